@@ -1,0 +1,409 @@
+"""Benchmark of the B200 grouped GEMM (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config L|E|...]
+
+Workload ("L"): a balanced MoE gate/up projection, B=8 experts per GPU,
+M=4096 tokens per expert, N=4096, K=7168, bf16 in / fp32 accumulate / bf16 out. Inputs are
+N(0,1), generated on the device (bf16), 940 MB per GPU, larger than the 126 MB L2, so no L2
+flush is needed between steps. A step is one grouped GEMM over all of the GPU's experts,
+enqueued through the C ABI (gg_run), timed back to back like the reference harness
+(bench/bench_main.cpp:490-501).
+
+Multi-GPU (torchrun, one process per GPU, NCCL only for the barrier and the max-over-ranks
+timing): experts are sharded contiguously (gg_expert_shard); every GPU keeps 8 experts, so the
+job grows with N ("scaling": "weak"). There is no collective on the GEMM path.
+
+`--impl reference` times the reference op's CPU fp32 path (the reference has no CPU
+implementation; the oracle port of its fp32 math runs on all host cores) on a bounded sample
+of the same workload, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "groupgemm-cktile-optimized_b200")
+
+METRIC = "grouped-GEMM TFLOPS/GPU (bf16) and % of B200 dense peak; aggregate at 1/2/4/8 GPU"
+DATASHEET_TFLOPS = 2250.0
+FALLBACK = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+
+CONFIGS = {
+    # name: (experts per GPU or total, M, N, K, dtype, sharding)
+    "L": dict(b=8, m=4096, n=4096, k=7168, dtype="bf16", per_gpu=True,
+              desc="L: B=8 experts per GPU, M=4096, N=4096, K=7168, bf16 (BASELINE configs[1])"),
+    "E": dict(b=256, m=512, n=4096, k=7168, dtype="bf16", per_gpu=False,
+              desc="E: B=256 experts sharded over the GPUs, M=512, N=4096, K=7168, bf16 (BASELINE configs[4])"),
+    "D": dict(b=32, m=2048, n=7168, k=2048, dtype="fp16", per_gpu=True,
+              desc="D: B=32 experts per GPU, M=2048, N=7168, K=2048, fp16 (BASELINE configs[2])"),
+    "P": dict(b=16, m=1000, n=2880, k=2880, dtype="bf16", per_gpu=True,
+              desc="P: B=16 experts per GPU, M=1000, N=2880, K=2880, bf16 (BASELINE configs[3])"),
+    "T": dict(b=4, m=256, n=512, k=384, dtype="bf16", per_gpu=True,
+              desc="T: B=4, M=256, N=512, K=384, bf16 (BASELINE configs[0])"),
+}
+
+
+def load_package():
+    spec = importlib.util.spec_from_file_location("gg_b200", os.path.join(PKG_DIR, "__init__.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["gg_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def load_oracle():
+    """CPU oracle: only the CPU-baseline leg and the reference arm use it."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # noqa: E402
+
+    return oracle
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK), "fallback"
+
+
+def shard_of(cfg, world, rank, gg):
+    """(global group count, [g0, g1) of this rank)."""
+    total = cfg["b"] * world if cfg["per_gpu"] else cfg["b"]
+    return total, gg.expert_shard(total, world, rank)
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML (read-only) every ~10 ms."""
+
+    REASONS = {
+        "hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+        "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+        "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+        "sw_power_cap": "nvmlClocksEventReasonSwPowerCap",
+        "hw_power_brake": "nvmlClocksEventReasonHwPowerBrakeSlowdown",
+    }
+
+    def __init__(self, device_index: int):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thr = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # NVML missing: report no clocks rather than fail the bench
+            self._nv = None
+            self.error = str(e)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for name, attr in self.REASONS.items():
+                    if r & getattr(nv, attr, 0):
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thr = threading.Thread(target=self._run, daemon=True)
+            self._thr.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._thr:
+            self._thr.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def cpu_baseline(cfg, budget_s: float = 10.0):
+    """Oracle port of the fp32 reference path on all host cores, on a bounded sample: the first
+    R rows of one expert against its full weight (2*R*N*K flop), R sized for ~budget_s."""
+    orc = load_oracle()
+    dt = 0 if cfg["dtype"] == "bf16" else 1
+    n, k = cfg["n"], cfg["k"]
+    threads = orc.hw_threads()
+    m = cfg["m"]
+    x, w = orc.make_inputs([m], n, k, dt)
+    probe = 16
+    t0 = time.perf_counter()
+    orc.grouped_gemm_f32(x, w, [m], dt, max_rows=probe, threads=threads)
+    dt_probe = time.perf_counter() - t0
+    rows = int(max(16, min(m, probe * budget_s / max(dt_probe, 1e-6))))
+    rows = rows // 16 * 16 or 16
+    t0 = time.perf_counter()
+    orc.grouped_gemm_f32(x, w, [m], dt, max_rows=rows, threads=threads)
+    el = time.perf_counter() - t0
+    flops = 2.0 * rows * n * k
+    return {"value": round(flops / el / 1e12, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
+            "sample": f"fp32 GEMM of {rows} rows x N={n} x K={k} of one expert ({flops / 1e9:.1f} GFLOP, "
+                      f"{el:.2f} s) with the oracle port on {threads} host threads"}
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    orc = load_oracle()
+    dt = 0 if cfg["dtype"] == "bf16" else 1
+    n, k, m = cfg["n"], cfg["k"], cfg["m"]
+    threads = orc.hw_threads()
+    x, w = orc.make_inputs([m], n, k, dt)
+    # bounded sample per step: rows of one expert sized for ~1.5 s per step
+    t0 = time.perf_counter()
+    orc.grouped_gemm_f32(x, w, [m], dt, max_rows=16, threads=threads)
+    rows = int(max(16, min(m, 16 * 1.5 / max(time.perf_counter() - t0, 1e-6)))) // 16 * 16 or 16
+    for _ in range(args.warmup):
+        orc.grouped_gemm_f32(x, w, [m], dt, max_rows=rows, threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        orc.grouped_gemm_f32(x, w, [m], dt, max_rows=rows, threads=threads)
+        times.append(time.perf_counter() - t0)
+    el = sum(times)
+    flops = 2.0 * rows * n * k * args.steps
+    value = flops / el / 1e12
+    sample = (f"each step: fp32 GEMM of {rows} rows x N={n} x K={k} of one expert of the {cfg['desc']} workload, "
+              f"oracle port of the reference's fp32 math on {threads} host threads")
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": "TFLOPS", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * el / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic N(0,1), reference generator",
+        "config": {"workload": cfg["desc"], "global_batch": cfg["b"] * cfg["m"], "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def load_traffic(cfg_name):
+    """Per-launch DRAM bytes of the kernel from the committed ncu summary (None if absent)."""
+    path = os.path.join(ROOT, "profiles", f"gg_sm100_{cfg_name}_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="L", choices=sorted(CONFIGS))
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--allgather", action="store_true", help="also time an NCCL all-gather of the outputs")
+    ap.add_argument("--variant", type=int, default=-1)
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.warmup < 3:
+        args.warmup = 3  # timing rule: at least 3 warm-up steps
+
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    gg = load_package()
+    dtype = gg.DTYPES[cfg["dtype"]]
+    tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
+    total_groups, (g0, g1) = shard_of(cfg, world, rank, gg)
+    ng = g1 - g0
+    m, n, k = cfg["m"], cfg["n"], cfg["k"]
+    group_m = [m] * ng
+    rows = m * ng
+    gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    x = torch.randn(rows, k, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
+    w = torch.empty(ng, n, k, device="cuda", dtype=tdt)
+    for g in range(ng):  # per expert to bound the fp32 temporary
+        w[g] = torch.randn(n, k, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
+    out = torch.empty(rows, n, device="cuda", dtype=tdt)
+    stream = torch.cuda.Stream()
+    s = stream.cuda_stream
+    backend = gg.make_b200_backend()
+    if args.variant >= 0:
+        backend.set_option("variant", args.variant)
+    why = backend.prepare(dtype, group_m, n, k, x.data_ptr(), w.data_ptr(), out.data_ptr(), s)
+    if why:
+        raise SystemExit(f"prepare refused the workload: {why}")
+    flops_rank = 2.0 * rows * n * k
+
+    # ---- device-timed steps (inputs resident in HBM) ----
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            backend.run(s)
+    torch.cuda.synchronize()
+    if backend.device_status(s) != 0:
+        raise SystemExit("kernel reported a bounded-wait timeout during warm-up")
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            backend.run(s)
+        ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms_total = ev0.elapsed_time(ev1)
+    if backend.device_status(s) != 0:
+        raise SystemExit("kernel reported a bounded-wait timeout in the timed region")
+    ms_step_rank = ms_total / args.steps
+    if dist:
+        t = torch.tensor([ms_step_rank], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_step = float(t.item())
+    else:
+        ms_step = ms_step_rank
+    total_flops = 2.0 * total_groups * m * n * k
+    value = total_flops / (ms_step * 1e-3) / 1e12
+
+    # ---- optional all-gather of the expert outputs (timed separately, not in value) ----
+    allgather = None
+    if args.allgather and dist:
+        gathered = torch.empty(world * rows, n, device="cuda", dtype=tdt)
+        for _ in range(2):
+            dist.all_gather_into_tensor(gathered, out)
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(5):
+            dist.all_gather_into_tensor(gathered, out)
+        a1.record()
+        a1.synchronize()
+        t = torch.tensor([a0.elapsed_time(a1) / 5], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        allgather = {"ms": round(float(t.item()), 4), "bytes_per_rank": rows * n * 2}
+        del gathered
+
+    # ---- end to end through the C ABI with host buffers ----
+    hx = torch.empty(x.shape, dtype=tdt, pin_memory=True)
+    hw = torch.empty(w.shape, dtype=tdt, pin_memory=True)
+    ho = torch.empty(out.shape, dtype=tdt, pin_memory=True)
+    hx.copy_(x)
+    hw.copy_(w)
+    torch.cuda.synchronize()
+    e2e_steps = max(1, min(args.e2e_steps, args.steps))
+    with torch.cuda.stream(stream):
+        for i in range(e2e_steps + 1):
+            if i == 1:
+                if dist:
+                    dist.barrier()
+                torch.cuda.synchronize()
+                ev0.record(stream)
+            x.copy_(hx, non_blocking=True)
+            w.copy_(hw, non_blocking=True)
+            backend.run(s)
+            ho.copy_(out, non_blocking=True)
+        ev1.record(stream)
+        ev1.synchronize()
+    e2e_ms = ev0.elapsed_time(ev1) / e2e_steps
+    if dist:
+        t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": round(total_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+           "h2d_bytes_per_step": int(hx.numel() * 2 + hw.numel() * 2), "d2h_bytes_per_step": int(ho.numel() * 2),
+           "ms_per_step": round(e2e_ms, 3), "steps": e2e_steps,
+           "path": "pinned host x,w -> device (cudaMemcpyAsync) -> gg_run -> out -> pinned host, per step"}
+
+    if dist:
+        dist.barrier()
+    if rank != 0:
+        backend.release()
+        if dist:
+            dist.destroy_process_group()
+        return 0
+
+    peaks, peak_src = measured_peaks()
+    achieved = flops_rank / (ms_step_rank * 1e-3) / 1e12
+    peak = float(peaks.get("bf16_tflops", FALLBACK["bf16_tflops"]))
+    traffic = load_traffic(args.config)
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} bf16 burst (cuBLAS)",
+                "frac_of_sustained": round(achieved / float(peaks.get("bf16_tflops_sustained", peak)), 4),
+                "frac_of_datasheet_2250": round(achieved / DATASHEET_TFLOPS, 4),
+                "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                "algorithmic_bytes": int(2 * (rows * k + ng * n * k + rows * n)),
+                "kernel": "gg::grouped_gemm_sm100 (" + backend.detail() + ")"}
+    if traffic:
+        roofline["traffic_source"] = traffic.get("source")
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak"
+        if cfg["per_gpu"] else "strong",
+        "vs_baseline": None, "dtype": cfg["dtype"],
+        "data": "synthetic N(0,1) (torch generator on the device), bf16; random expert weights",
+        "config": {"workload": cfg["desc"], "global_batch": total_groups * m, "experts": total_groups,
+                   "parallelism": f"ep{world}", "l2": "inputs larger than L2 (no flush)",
+                   "per_gpu_tflops": round(value / world, 2),
+                   "pct_of_datasheet_dense_peak": round(100 * value / world / DATASHEET_TFLOPS, 2)},
+        "roofline": roofline,
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+        "detail": backend.detail(),
+    }
+    if allgather:
+        line["allgather"] = allgather
+    backend.release()
+    del x, w, out
+    torch.cuda.empty_cache()
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg)
+    print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,428 @@
+// Host side of the B200 grouped-GEMM backend: the C ABI of include/gg_b200.h.
+//
+// gg_prepare() plays the role of CkTileBackend::prepare_typed + finish
+// (ck_kernel/ck_grouped_gemm.cpp:153-218): it validates the problem, builds the per-group
+// argument buffer on the device (tile and row offsets instead of CK's GemmTransKernelArg
+// array), encodes the TMA descriptors, picks the kernel variant and sizes the persistent grid.
+// gg_run() is the single launch of CkGroupedGemm::launch (ck_kernel/ck_grouped_gemm.cpp:114-121).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "gg_b200.h"
+#include "gg_kernel.cuh"
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// One compiled instance of the kernel.
+struct Variant {
+    int cg;        // CTAs per tile (1 or 2)
+    int bn;        // tile N
+    int cluster_m; // tile M
+    int stages;
+    int smem;
+    const void *fn_bf16;
+    const void *fn_fp16;
+};
+
+template <int kCG, int kBN> Variant make_variant() {
+    using C = gg::TileCfg<kCG, kBN>;
+    return Variant{kCG,
+                   kBN,
+                   C::kClusterM,
+                   C::kStages,
+                   C::kSmemBytes,
+                   reinterpret_cast<const void *>(&gg::grouped_gemm_sm100<__nv_bfloat16, kCG, kBN>),
+                   reinterpret_cast<const void *>(&gg::grouped_gemm_sm100<__half, kCG, kBN>)};
+}
+
+const Variant &variant_at(int i) {
+    static const Variant v[3] = {make_variant<2, 256>(), make_variant<1, 256>(), make_variant<1, 128>()};
+    return v[i];
+}
+constexpr int kNumVariants = 3;
+
+}  // namespace
+
+struct gg_handle {
+    // options
+    int opt_variant = -1;
+    int opt_band = 0;
+    int opt_max_ctas = 0;
+    int64_t opt_timeout_ms = 2000;
+
+    // prepared state
+    bool ready = false;
+    int device = -1;
+    int dtype = 0;
+    int variant = 0;
+    int64_t total_m = 0;
+    int32_t *d_meta = nullptr;  // tile_off[G+1] then row_off[G+1]
+    size_t meta_cap = 0;        // int32 entries
+    uint32_t *d_status = nullptr;
+    CUtensorMap tmap_a{}, tmap_b{};
+    gg::KernelParams params{};
+    int grid = 0;
+    const void *fn = nullptr;
+    int smem = 0;
+    int cg = 1;
+
+    std::string detail, last_error;
+};
+
+namespace {
+
+int fail(gg_handle *h, int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    h->last_error = buf;
+    return code;
+}
+
+int refuse(gg_handle *h, char *why, size_t why_len, const char *msg) {
+    h->last_error = msg;
+    if (why && why_len > 0) {
+        std::strncpy(why, msg, why_len - 1);
+        why[why_len - 1] = '\0';
+    }
+    return GG_NOT_SUPPORTED;
+}
+
+#define GG_CUDA(h, expr)                                                                                  \
+    do {                                                                                                  \
+        cudaError_t e_ = (expr);                                                                          \
+        if (e_ != cudaSuccess)                                                                            \
+            return fail((h), GG_ERR_CUDA, "%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__); \
+    } while (0)
+
+int64_t tiles_for(const gg_problem *p, const Variant &v) {
+    const int64_t tn = (p->n + v.bn - 1) / v.bn;
+    int64_t t = 0;
+    for (int g = 0; g < p->group_num; ++g)
+        t += (p->group_m[g] + v.cluster_m - 1) / v.cluster_m * tn;
+    return t;
+}
+
+// Automatic variant choice: the largest tile that still gives every SM (pair) work; smaller
+// tiles only for low-tile-count shapes (the reference loses there, README.md:56-58).
+int choose_variant(const gg_problem *p, int num_sms) {
+    const int64_t t0 = tiles_for(p, variant_at(0));
+    if (t0 >= int64_t(num_sms / 2) * 3 / 4)
+        return 0;
+    const int64_t t1 = tiles_for(p, variant_at(1));
+    if (t1 >= int64_t(num_sms) * 3 / 4)
+        return 1;
+    return 2;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gg_abi_version(void) { return 1; }
+
+gg_handle *gg_create(void) { return new (std::nothrow) gg_handle(); }
+
+const char *gg_name(const gg_handle *) { return "b200"; }
+
+const char *gg_detail(const gg_handle *h) { return h ? h->detail.c_str() : ""; }
+
+const char *gg_last_error(const gg_handle *h) { return h ? h->last_error.c_str() : "null handle"; }
+
+int gg_set_option(gg_handle *h, const char *key, int64_t value) {
+    if (!h || !key)
+        return GG_ERR_ARG;
+    if (!std::strcmp(key, "variant")) {
+        if (value < -1 || value >= kNumVariants)
+            return fail(h, GG_ERR_ARG, "variant must be -1..%d", kNumVariants - 1);
+        h->opt_variant = int(value);
+    } else if (!std::strcmp(key, "band")) {
+        if (value < 0 || value > 1024)
+            return fail(h, GG_ERR_ARG, "band must be 0..1024");
+        h->opt_band = int(value);
+    } else if (!std::strcmp(key, "max_ctas")) {
+        if (value < 0)
+            return fail(h, GG_ERR_ARG, "max_ctas must be >= 0");
+        h->opt_max_ctas = int(value);
+    } else if (!std::strcmp(key, "timeout_ms")) {
+        if (value < 1 || value > 60000)
+            return fail(h, GG_ERR_ARG, "timeout_ms must be 1..60000");
+        h->opt_timeout_ms = value;
+    } else {
+        return fail(h, GG_ERR_ARG, "unknown option '%s'", key);
+    }
+    return GG_OK;
+}
+
+void gg_release(gg_handle *h) {
+    if (!h)
+        return;
+    if (h->d_meta)
+        cudaFree(h->d_meta);
+    if (h->d_status)
+        cudaFree(h->d_status);
+    h->d_meta = nullptr;
+    h->d_status = nullptr;
+    h->meta_cap = 0;
+    h->ready = false;
+    h->detail.clear();
+}
+
+void gg_destroy(gg_handle *h) {
+    if (!h)
+        return;
+    gg_release(h);
+    delete h;
+}
+
+int gg_expert_shard(int32_t group_num, int32_t world, int32_t rank, int32_t *g0, int32_t *g1) {
+    if (group_num < 0 || world < 1 || rank < 0 || rank >= world || !g0 || !g1)
+        return GG_ERR_ARG;
+    const int32_t base = group_num / world, extra = group_num % world;
+    *g0 = rank * base + std::min(rank, extra);
+    *g1 = *g0 + base + (rank < extra ? 1 : 0);
+    return GG_OK;
+}
+
+int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why, size_t why_len) {
+    if (!h)
+        return GG_ERR_ARG;
+    h->ready = false;
+    h->last_error.clear();
+    if (why && why_len)
+        why[0] = '\0';
+    if (!p)
+        return fail(h, GG_ERR_ARG, "null problem");
+
+    // ---- argument checks (host only; an unsupported shape is an N/A, not an error) ----
+    if (p->dtype != GG_BF16 && p->dtype != GG_FP16)
+        return refuse(h, why, why_len, "dtype must be bf16 (0) or fp16 (1)");
+    if (p->group_num < 1)
+        return refuse(h, why, why_len, "group_num must be >= 1");
+    if (!p->group_m)
+        return refuse(h, why, why_len, "group_m is null");
+    if (p->n < 1 || p->k < 1)
+        return refuse(h, why, why_len, "n and k must be >= 1");
+    if (p->k % 8 != 0)
+        return refuse(h, why, why_len, "k must be a multiple of 8 (16-byte TMA row stride)");
+    if (p->n % 8 != 0)
+        return refuse(h, why, why_len, "n must be a multiple of 8 (16-byte output row stride)");
+    if (p->n > (int64_t(1) << 30) || p->k > (int64_t(1) << 30))
+        return refuse(h, why, why_len, "n and k must be below 2^30");
+    int64_t total_m = 0;
+    for (int g = 0; g < p->group_num; ++g) {
+        if (p->group_m[g] < 0)
+            return refuse(h, why, why_len, "group_m entries must be >= 0");
+        total_m += p->group_m[g];
+        if (total_m >= (int64_t(1) << 31))
+            return refuse(h, why, why_len, "sum(group_m) must be below 2^31");
+    }
+    if (total_m > 0 && (!p->x || !p->w || !p->out))
+        return refuse(h, why, why_len, "x, w and out must be non-null device pointers");
+    if ((reinterpret_cast<uintptr_t>(p->x) | reinterpret_cast<uintptr_t>(p->w) |
+         reinterpret_cast<uintptr_t>(p->out)) & 15u)
+        return refuse(h, why, why_len, "x, w and out must be 16-byte aligned");
+    if (int64_t(p->group_num) * p->n * p->k >= (int64_t(1) << 40) / 2)
+        return refuse(h, why, why_len, "weight tensor too large for one TMA descriptor");
+
+    // ---- device + variant ----
+    int dev = 0;
+    GG_CUDA(h, cudaGetDevice(&dev));
+    int num_sms = 0, cc_major = 0, cc_minor = 0;
+    GG_CUDA(h, cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev));
+    GG_CUDA(h, cudaDeviceGetAttribute(&cc_major, cudaDevAttrComputeCapabilityMajor, dev));
+    GG_CUDA(h, cudaDeviceGetAttribute(&cc_minor, cudaDevAttrComputeCapabilityMinor, dev));
+    if (cc_major != 10 || cc_minor != 0)
+        return refuse(h, why, why_len, "needs an sm_100 GPU (B200/GB200)");
+    EncodeTiledFn encode = get_encode_fn();
+    if (!encode)
+        return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
+
+    const int vi = h->opt_variant >= 0 ? h->opt_variant : choose_variant(p, num_sms);
+    const Variant &v = variant_at(vi);
+    const void *fn = p->dtype == GG_BF16 ? v.fn_bf16 : v.fn_fp16;
+
+    // ---- group arguments: tile offsets (this variant's tile) and row offsets ----
+    const int G = p->group_num;
+    const int64_t tiles_n = (p->n + v.bn - 1) / v.bn;
+    std::vector<int32_t> meta(2 * size_t(G + 1));
+    int64_t tiles = 0, rows = 0;
+    for (int g = 0; g < G; ++g) {
+        meta[g] = int32_t(tiles);
+        meta[G + 1 + g] = int32_t(rows);
+        tiles += (p->group_m[g] + v.cluster_m - 1) / v.cluster_m * tiles_n;
+        rows += p->group_m[g];
+        if (tiles >= (int64_t(1) << 31))
+            return refuse(h, why, why_len, "too many tiles");
+    }
+    meta[G] = int32_t(tiles);
+    meta[2 * G + 1] = int32_t(rows);
+
+    if (h->meta_cap < meta.size()) {
+        if (h->d_meta)
+            cudaFree(h->d_meta);
+        h->d_meta = nullptr;
+        h->meta_cap = 0;
+        GG_CUDA(h, cudaMalloc(&h->d_meta, meta.size() * sizeof(int32_t)));
+        h->meta_cap = meta.size();
+    }
+    if (!h->d_status)
+        GG_CUDA(h, cudaMalloc(&h->d_status, 16));
+    GG_CUDA(h, cudaMemsetAsync(h->d_status, 0, 16, stream));
+    GG_CUDA(h, cudaMemcpyAsync(h->d_meta, meta.data(), meta.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                               stream));
+
+    // ---- TMA descriptors ----
+    const CUtensorMapDataType dt =
+        p->dtype == GG_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (total_m > 0) {
+        const cuuint64_t a_dim[2] = {cuuint64_t(p->k), cuuint64_t(total_m)};
+        const cuuint64_t a_stride[1] = {cuuint64_t(p->k) * 2};
+        const cuuint32_t a_box[2] = {gg::kBK, gg::kBM};
+        const cuuint32_t estride[3] = {1, 1, 1};
+        CUresult r = encode(&h->tmap_a, dt, 2, const_cast<void *>(p->x), a_dim, a_stride, a_box, estride,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS)
+            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed: %d", int(r));
+        const cuuint64_t b_dim[3] = {cuuint64_t(p->k), cuuint64_t(p->n), cuuint64_t(G)};
+        const cuuint64_t b_stride[2] = {cuuint64_t(p->k) * 2, cuuint64_t(p->n) * cuuint64_t(p->k) * 2};
+        const cuuint32_t b_box[3] = {gg::kBK, cuuint32_t(v.bn / v.cg), 1};
+        r = encode(&h->tmap_b, dt, 3, const_cast<void *>(p->w), b_dim, b_stride, b_box, estride,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS)
+            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(w) failed: %d", int(r));
+    }
+
+    // ---- raster band and persistent grid ----
+    int band = h->opt_band;
+    if (band <= 0) {
+        // Enough m-tiles per band that one wave of tiles spans few weight panels.
+        band = v.cg == 2 ? 8 : 16;
+    }
+    GG_CUDA(h, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem));
+    int slots = 0;  // CTAs that can be resident at once
+    if (v.cg == 2) {
+        cudaLaunchConfig_t cfg{};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(num_sms, 1, 1);
+        cfg.blockDim = dim3(gg::kThreads, 1, 1);
+        cfg.dynamicSmemBytes = size_t(v.smem);
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        GG_CUDA(h, cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg));
+        slots = 2 * clusters;
+    } else {
+        slots = num_sms;
+    }
+    if (h->opt_max_ctas > 0)
+        slots = std::min(slots, std::max(v.cg, h->opt_max_ctas / v.cg * v.cg));
+    if (slots < v.cg)
+        return refuse(h, why, why_len, "no CTA of this kernel fits on the device");
+    const int64_t want = tiles * v.cg;
+    h->grid = int(std::max<int64_t>(v.cg, std::min<int64_t>(slots, want)));
+
+    gg::KernelParams &kp = h->params;
+    kp.tile_off = h->d_meta;
+    kp.row_off = h->d_meta + (G + 1);
+    kp.out = p->out;
+    kp.status = h->d_status;
+    kp.group_num = G;
+    kp.n = int32_t(p->n);
+    kp.k = int32_t(p->k);
+    kp.num_kb = int32_t((p->k + gg::kBK - 1) / gg::kBK);
+    kp.tiles_n = int32_t(tiles_n);
+    kp.total_tiles = int32_t(tiles);
+    kp.band = band;
+    kp.timeout_ns = uint64_t(h->opt_timeout_ms) * 1000000ull;
+
+    GG_CUDA(h, cudaStreamSynchronize(stream));
+
+    h->device = dev;
+    h->dtype = p->dtype;
+    h->variant = vi;
+    h->total_m = total_m;
+    h->fn = fn;
+    h->smem = v.smem;
+    h->cg = v.cg;
+    char d[256];
+    std::snprintf(d, sizeof(d), "gg_sm100<%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld grid=%d band=%d",
+                  p->dtype == GG_BF16 ? "bf16" : "fp16", v.cluster_m, v.bn, gg::kBK, v.cg, v.stages,
+                  (long long)tiles, h->grid, band);
+    h->detail = d;
+    h->ready = true;
+    return GG_OK;
+}
+
+int gg_run(gg_handle *h, gg_stream_t stream) {
+    if (!h)
+        return GG_ERR_ARG;
+    if (!h->ready)
+        return fail(h, GG_ERR_ARG, "gg_run before a successful gg_prepare");
+    if (h->params.total_tiles == 0)
+        return GG_OK;  // every group empty: nothing to write
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(h->cg);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(unsigned(h->grid), 1, 1);
+    cfg.blockDim = dim3(gg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = size_t(h->smem);
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *args[3] = {&h->tmap_a, &h->tmap_b, &h->params};
+    GG_CUDA(h, cudaLaunchKernelExC(&cfg, h->fn, args));
+    return GG_OK;
+}
+
+int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status) {
+    if (!h || !status)
+        return GG_ERR_ARG;
+    *status = 0;
+    if (!h->d_status)
+        return GG_OK;
+    GG_CUDA(h, cudaStreamSynchronize(stream));
+    GG_CUDA(h, cudaMemcpy(status, h->d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost));
+    GG_CUDA(h, cudaMemset(h->d_status, 0, sizeof(uint32_t)));
+    if (*status != 0)
+        return fail(h, GG_ERR_DEVICE, "kernel bounded wait timed out: status 0x%x", *status);
+    return GG_OK;
+}
+
+}  // extern "C"

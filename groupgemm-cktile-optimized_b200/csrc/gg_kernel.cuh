@@ -1,0 +1,389 @@
+// Persistent, warp-specialised grouped GEMM for sm_100a (B200):
+//
+//     out[rows of group g] = x[rows of group g] @ w[g]^T      (RCR, fp32 accumulate)
+//
+//   x   [sum(M_g), K] row-major  -- A operand, K-major
+//   w   [G, N, K]     row-major  -- B operand, K-major
+//   out [sum(M_g), N] row-major
+//
+// This replaces the reference's CK Tile GroupedGemmKernel + HandPipelineAsmS main loop +
+// FastEpilogue (ck_kernel/ck_grouped_gemm.cpp:34-124, ck_kernel/hand_pipeline_asm_s.hpp:157-357,
+// ck_kernel/fast_epilogue.hpp:29-118) with a Blackwell design:
+//
+//   * one CTA per SM (kCG = 1) or one CTA pair per two SMs (kCG = 2, tcgen05 cta_group::2),
+//     persistent over a static tile schedule that covers every group (the scheduler is on the
+//     device: a tile index is mapped to (group, m-tile, n-tile) from per-group tile offsets);
+//   * warp 0: TMA producer. 128-byte-swizzled A (128 x 64) and B (BN/kCG x 64) tiles into a
+//     STAGES-deep shared-memory ring guarded by full/empty mbarriers (no multicast: every CTA
+//     loads its own halves);
+//   * warp 1: TMEM allocator and, in the pair leader, the single MMA-issuing thread. The
+//     accumulator lives in Tensor Memory, double-buffered (2 x BN fp32 columns) so the
+//     epilogue of tile i overlaps the main loop of tile i+1;
+//   * warps 2-5: epilogue. tcgen05.ld 32 lanes x 32 columns, fp32 -> bf16/fp16 (RNE),
+//     row/column-masked 16-byte streaming stores (evict-first, the analogue of the
+//     reference's non-temporal C stores, ck_kernel/coherence_epilogue.hpp:17-30).
+//
+// Tails: TMA zero-fills reads past the tensor ends (K tail, N tail via the 3-D weight map,
+// rows past sum(M)). A tile that runs past its group's last row reads the next group's rows;
+// those accumulator rows are never stored. There is no K % 64 restriction (the reference
+// refuses one, ck_kernel/ck_grouped_gemm.cpp:191-193).
+//
+// Every wait is bounded. A wait that runs out sets a device status word (role and barrier)
+// and all roles leave their loops; the kernel then frees its Tensor Memory and returns.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cstdint>
+
+#include "gg_ptx.cuh"
+
+namespace gg {
+
+constexpr int kThreads = 192;  // 6 warps: producer, MMA, 4 x epilogue
+constexpr int kBM = 128;       // accumulator rows per CTA (TMEM lanes)
+constexpr int kBK = 64;        // K per stage: one 128-byte swizzle row of 16-bit elements
+constexpr int kUmmaK = 16;     // K per tcgen05.mma (kind::f16)
+constexpr int kSmemBudget = 200 * 1024;
+
+// Status word values (0 = ok). Timeouts encode role (bits 8-11) and barrier (bits 0-7).
+enum : uint32_t {
+    kStatusTimeout = 0x1000u,
+    kRoleProducer = 1u << 8,
+    kRoleMma = 2u << 8,
+    kRoleEpilogue = 3u << 8,
+};
+
+struct KernelParams {
+    const int32_t *tile_off;  // [G+1] first tile of each group (cluster tiles)
+    const int32_t *row_off;   // [G+1] first row of each group in x / out
+    void *out;
+    uint32_t *status;
+    int32_t group_num;
+    int32_t n;
+    int32_t k;
+    int32_t num_kb;       // ceil(K / 64)
+    int32_t tiles_n;      // ceil(N / BN)
+    int32_t total_tiles;  // tile_off[G]
+    int32_t band;         // M tiles per raster band (L2 reuse of the weight panel)
+    int32_t pad_;
+    uint64_t timeout_ns;
+};
+
+template <typename T> struct Fmt;
+template <> struct Fmt<__nv_bfloat16> {
+    static constexpr uint32_t kUmma = 1;
+};
+template <> struct Fmt<__half> {
+    static constexpr uint32_t kUmma = 0;
+};
+
+template <int kCG, int kBN> struct TileCfg {
+    static_assert(kCG == 1 || kCG == 2, "CTA group of 1 or 2");
+    static_assert(kBN % 16 == 0 && kBN >= 32 && kBN <= 256, "UMMA N");
+    static constexpr int kClusterM = kBM * kCG;  // rows per (cluster) tile
+    static constexpr int kBRows = kBN / kCG;     // weight rows each CTA loads
+    static constexpr int kABytes = kBM * kBK * 2;
+    static constexpr int kBBytes = kBRows * kBK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
+    static constexpr int kTmemCols = (2 * kBN) <= 32 ? 32 : (2 * kBN) <= 64 ? 64 : (2 * kBN) <= 128 ? 128
+                                     : (2 * kBN) <= 256 ? 256 : 512;
+    // barriers: full[S], empty[S], tmem_full[2], tmem_empty[2]; then tmem ptr and abort flag
+    static constexpr int kBarOffset = kStages * kStageBytes;
+    static constexpr int kSmemBytes = kBarOffset + (2 * kStages + 4) * 8 + 16 + 1024;  // + align slack
+    static_assert(kStages >= 2, "ring too shallow");
+};
+
+struct TileCoord {
+    int g, mt, nt;
+};
+
+// Map a linear tile index to (group, m-tile, n-tile). Within a group, tiles are rastered in
+// bands of `band` m-tiles: all n-tiles of a band are visited m-fastest, so concurrently
+// running tiles share one weight panel (n-tile) and the band's activation rows stay in L2 —
+// the role CK's GemmSpatiallyLocalTilePartitioner<8,4> plays in the reference
+// (ck_kernel/ck_grouped_gemm_config.hpp:74-77).
+template <int kClusterM>
+__device__ __forceinline__ TileCoord decode_tile(const KernelParams &p, int t, int &cursor) {
+    while (__ldg(&p.tile_off[cursor + 1]) <= t)
+        ++cursor;
+    const int g = cursor;
+    const int local = t - __ldg(&p.tile_off[g]);
+    const int m = __ldg(&p.row_off[g + 1]) - __ldg(&p.row_off[g]);
+    const int tiles_m = (m + kClusterM - 1) / kClusterM;
+    const int band_tiles = p.band * p.tiles_n;
+    const int b = local / band_tiles;
+    const int r = local - b * band_tiles;
+    const int rows = min(p.band, tiles_m - b * p.band);
+    const int nt = r / rows;
+    const int mt = b * p.band + (r - nt * rows);
+    return {g, mt, nt};
+}
+
+struct Abort {
+    uint32_t *status;         // global
+    volatile uint32_t *flag;  // this CTA's shared abort flag
+    uint64_t timeout_ns;
+};
+
+// Bounded wait by one lane. Returns false if this or another role gave up.
+__device__ __noinline__ bool wait_lane(uint32_t bar, uint32_t parity, const Abort &ab, uint32_t code) {
+    if (ptx::mbar_try_wait(bar, parity))
+        return true;
+    const uint64_t t0 = ptx::globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (ptx::mbar_try_wait(bar, parity))
+            return true;
+        if ((it & 31u) == 0) {
+            if (*ab.flag != 0u || *(volatile uint32_t *)ab.status != 0u) {
+                *ab.flag = 1u;
+                return false;
+            }
+            if (ptx::globaltimer() - t0 > ab.timeout_ns) {
+                atomicCAS(ab.status, 0u, code);
+                *ab.flag = 1u;
+                return false;
+            }
+        }
+    }
+}
+
+// Warp-uniform bounded wait: lane 0 waits, the result is broadcast.
+__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, const Abort &ab, uint32_t code) {
+    int ok = 1;
+    if (ptx::lane_id() == 0)
+        ok = wait_lane(bar, parity, ab, code) ? 1 : 0;
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(uint32_t a, uint32_t b) {
+    if constexpr (sizeof(T) == 2 && Fmt<T>::kUmma == 1) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(__uint_as_float(a), __uint_as_float(b));
+        return *reinterpret_cast<uint32_t *>(&v);
+    } else {
+        __half2 v = __floats2half2_rn(__uint_as_float(a), __uint_as_float(b));
+        return *reinterpret_cast<uint32_t *>(&v);
+    }
+}
+
+template <typename T, int kCG, int kBN>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_sm100(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                       const __grid_constant__ KernelParams p) {
+    using C = TileCfg<kCG, kBN>;
+    constexpr uint32_t kIdesc = ptx::f16_idesc(Fmt<T>::kUmma, kBM * kCG, kBN);
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-byte alignment for the 128-byte swizzle atoms.
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t smem_base = ptx::smem_addr(smem);
+    const uint32_t bar_base = smem_base + C::kBarOffset;
+    auto full_bar = [&](int s) { return bar_base + 8u * s; };
+    auto empty_bar = [&](int s) { return bar_base + 8u * (C::kStages + s); };
+    auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * C::kStages + a); };
+    auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * C::kStages + 2 + a); };
+    uint32_t *tmem_ptr_slot = reinterpret_cast<uint32_t *>(smem + C::kBarOffset + (2 * C::kStages + 4) * 8);
+    volatile uint32_t *abort_flag = tmem_ptr_slot + 1;
+
+    const int warp = threadIdx.x / 32;
+    const uint32_t lane = threadIdx.x % 32;
+    const uint32_t cta_rank = kCG == 2 ? ptx::cluster_ctarank() : 0u;
+    const bool leader = cta_rank == 0;
+    const int cluster_id = blockIdx.x / kCG;
+    const int num_clusters = gridDim.x / kCG;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            ptx::mbar_init(full_bar(s), 1);   // leader producer's arrive.expect_tx
+            ptx::mbar_init(empty_bar(s), 1);  // one tcgen05.commit per use
+        }
+        for (int a = 0; a < 2; ++a) {
+            ptx::mbar_init(tfull_bar(a), 1);         // one tcgen05.commit per tile
+            ptx::mbar_init(tempty_bar(a), 4 * kCG);  // one arrive per epilogue warp of the pair
+        }
+        *abort_flag = 0u;
+        ptx::fence_mbar_init();
+        ptx::fence_proxy_async_smem();
+    }
+    if (warp == 0 && lane == 0) {
+        ptx::prefetch_tmap(&tmap_a);
+        ptx::prefetch_tmap(&tmap_b);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc<kCG>(ptx::smem_addr(tmem_ptr_slot), C::kTmemCols);
+        ptx::tmem_relinquish<kCG>();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if constexpr (kCG == 2)
+        ptx::cluster_sync();  // peer barriers are initialised before any remote arrive
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = *tmem_ptr_slot;
+
+    const Abort ab{p.status, abort_flag, p.timeout_ns};
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        const uint32_t full_leader0 = kCG == 2 ? ptx::mapa(full_bar(0), 0) : full_bar(0);
+        int cursor = 0;
+        uint32_t it = 0;
+        bool ok = true;
+        for (int t = cluster_id; t < p.total_tiles && ok; t += num_clusters) {
+            const TileCoord tc = decode_tile<C::kClusterM>(p, t, cursor);
+            const int a_row = __ldg(&p.row_off[tc.g]) + tc.mt * C::kClusterM + int(cta_rank) * kBM;
+            const int b_row = tc.nt * kBN + int(cta_rank) * C::kBRows;
+            for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+                const int s = int(it % C::kStages);
+                const uint32_t ph = (it / C::kStages) & 1u;
+                if (!wait_warp(empty_bar(s), ph ^ 1u, ab, kStatusTimeout | kRoleProducer | uint32_t(s))) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t a_dst = smem_base + uint32_t(s) * C::kStageBytes;
+                    const uint32_t b_dst = a_dst + C::kABytes;
+                    const uint32_t fb = full_leader0 + 8u * s;
+                    if (leader)
+                        ptx::mbar_arrive_expect_tx(full_bar(s), uint32_t(kCG * C::kStageBytes));
+                    if constexpr (kCG == 1) {
+                        ptx::tma_load_2d(a_dst, &tmap_a, fb, kb * kBK, a_row);
+                        ptx::tma_load_3d(b_dst, &tmap_b, fb, kb * kBK, b_row, tc.g);
+                    } else {
+                        ptx::tma_load_2d_pair(a_dst, &tmap_a, fb, kb * kBK, a_row);
+                        ptx::tma_load_3d_pair(b_dst, &tmap_b, fb, kb * kBK, b_row, tc.g);
+                    }
+                }
+                __syncwarp();
+            }
+        }
+        // Tail: every stage released, so no tcgen05.commit is still in flight to this CTA.
+        for (uint32_t i = it; ok && i < it + C::kStages; ++i)
+            ok = wait_warp(empty_bar(int(i % C::kStages)), ((i / C::kStages) & 1u) ^ 1u, ab,
+                           kStatusTimeout | kRoleProducer | 0x80u);
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (pair leader only) ----------------
+        if (leader) {
+            int cursor = 0;
+            uint32_t it = 0, tl = 0;
+            bool ok = true;
+            for (int t = cluster_id; t < p.total_tiles && ok; t += num_clusters, ++tl) {
+                (void)decode_tile<C::kClusterM>(p, t, cursor);
+                const int acc = int(tl & 1u);
+                const uint32_t acc_ph = (tl >> 1) & 1u;
+                if (!wait_warp(tempty_bar(acc), acc_ph ^ 1u, ab, kStatusTimeout | kRoleMma | 0x40u | uint32_t(acc))) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + uint32_t(acc * kBN);
+                for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+                    const int s = int(it % C::kStages);
+                    const uint32_t ph = (it / C::kStages) & 1u;
+                    if (!wait_warp(full_bar(s), ph, ab, kStatusTimeout | kRoleMma | uint32_t(s))) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t a_addr = smem_base + uint32_t(s) * C::kStageBytes;
+                        const uint32_t b_addr = a_addr + C::kABytes;
+                        const uint64_t adesc = ptx::sw128_kmajor_desc(a_addr);
+                        const uint64_t bdesc = ptx::sw128_kmajor_desc(b_addr);
+#pragma unroll
+                        for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+                            // advance 16 elements (32 bytes) along K inside the swizzle atom
+                            ptx::umma_f16<kCG>(d_tmem, adesc + uint64_t(kk * 2), bdesc + uint64_t(kk * 2), kIdesc,
+                                               (kb | kk) != 0 ? 1u : 0u);
+                        }
+                        ptx::umma_commit<kCG>(empty_bar(s));
+                        if constexpr (kCG == 2)
+                            ptx::umma_commit<kCG>(ptx::mapa(empty_bar(s), 1));
+                    }
+                    __syncwarp();
+                }
+                if (!ok)
+                    break;
+                if (lane == 0) {
+                    ptx::umma_commit<kCG>(tfull_bar(acc));
+                    if constexpr (kCG == 2)
+                        ptx::umma_commit<kCG>(ptx::mapa(tfull_bar(acc), 1));
+                }
+                __syncwarp();
+            }
+            // Tail: both accumulators released by every epilogue warp of the pair.
+            for (uint32_t i = tl; ok && i < tl + 2; ++i)
+                ok = wait_warp(tempty_bar(int(i & 1u)), ((i >> 1) & 1u) ^ 1u, ab, kStatusTimeout | kRoleMma | 0x80u);
+        }
+    } else {
+        // ---------------- epilogue (4 warps) ----------------
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int row_in_cta = q * 32 + int(lane);
+        const uint32_t tempty_leader0 = kCG == 2 ? ptx::mapa(tempty_bar(0), 0) : tempty_bar(0);
+        T *out = static_cast<T *>(p.out);
+        int cursor = 0;
+        uint32_t tl = 0;
+        for (int t = cluster_id; t < p.total_tiles; t += num_clusters, ++tl) {
+            const TileCoord tc = decode_tile<C::kClusterM>(p, t, cursor);
+            const int acc = int(tl & 1u);
+            const uint32_t acc_ph = (tl >> 1) & 1u;
+            if (!wait_warp(tfull_bar(acc), acc_ph, ab, kStatusTimeout | kRoleEpilogue | uint32_t(acc)))
+                break;
+            ptx::tc_fence_after();
+            const int g_row0 = __ldg(&p.row_off[tc.g]);
+            const int m = __ldg(&p.row_off[tc.g + 1]) - g_row0;
+            const int local_row = tc.mt * C::kClusterM + int(cta_rank) * kBM + row_in_cta;
+            const bool row_ok = local_row < m;
+            T *orow = out + (int64_t(g_row0) + local_row) * p.n;
+            const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * kBN);
+#pragma unroll 1
+            for (int c = 0; c < kBN / 32; ++c) {
+                uint32_t r[32];
+                ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
+                ptx::tmem_wait_ld(r);
+                const int col = tc.nt * kBN + c * 32;
+                if (row_ok) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (col + j * 8 < p.n) {
+                            uint4 v;
+                            v.x = pack2<T>(r[8 * j + 0], r[8 * j + 1]);
+                            v.y = pack2<T>(r[8 * j + 2], r[8 * j + 3]);
+                            v.z = pack2<T>(r[8 * j + 4], r[8 * j + 5]);
+                            v.w = pack2<T>(r[8 * j + 6], r[8 * j + 7]);
+                            __stcs(reinterpret_cast<uint4 *>(orow + col + j * 8), v);
+                        }
+                    }
+                }
+            }
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if constexpr (kCG == 2)
+                    ptx::mbar_arrive_cluster(tempty_leader0 + 8u * acc);
+                else
+                    ptx::mbar_arrive(tempty_bar(acc));
+            }
+        }
+    }
+
+    // ---------------- teardown ----------------
+    if (*abort_flag != 0u) {
+        // Let copies and MMAs already issued drain before the memory they target goes away.
+        const uint64_t t0 = ptx::globaltimer();
+        while (ptx::globaltimer() - t0 < 200000ull)
+            __nanosleep(1000);
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if constexpr (kCG == 2)
+        ptx::cluster_sync();  // no remote arrive or MMA still targets either CTA
+    ptx::tc_fence_after();
+    if (warp == 1)
+        ptx::tmem_dealloc<kCG>(tmem_base, C::kTmemCols);
+}
+
+}  // namespace gg

@@ -1,0 +1,124 @@
+/*
+ * gg_b200.h — C ABI of the B200 (sm_100a) grouped-GEMM backend.
+ *
+ * Operation (forward MoE grouped GEMM, RCR layout), the op of the reference's
+ * GroupedGemmProblem (common/backend.hpp:32-60):
+ *
+ *     out[rows of group g] = x[rows of group g] @ w[g]^T
+ *     x   [sum(group_m), k]  row-major   (tokens of all experts, back to back)
+ *     w   [group_num, n, k]  row-major   (one weight matrix per expert)
+ *     out [sum(group_m), n]  row-major
+ *     bf16 or fp16 in, fp32 accumulation, output in the input dtype.
+ *
+ * The entry points mirror the reference's `class Backend` (common/backend.hpp:62-79):
+ * prepare() is untimed set-up that returns "" or a reason the shape cannot run, run() enqueues
+ * exactly one grouped GEMM without synchronising, release() frees what prepare() allocated.
+ * Instead of exiting on a device error (TUNEMAX_HIP_CHECK, common/backend.hpp:15-23) every call
+ * returns a status code and the library never terminates the process.
+ *
+ * Plain pointers and sizes only. `gg_stream_t` is the same type as CUDA's cudaStream_t
+ * (NULL = the legacy default stream). A handle is bound to the device that is current when
+ * gg_prepare() is called; it is not thread-safe (one handle per thread and device).
+ */
+#ifndef GG_B200_H
+#define GG_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *gg_stream_t; /* == cudaStream_t */
+typedef struct gg_handle gg_handle;
+
+/* Element types (tunemax::DType, common/backend.hpp:27). */
+enum gg_dtype { GG_BF16 = 0, GG_FP16 = 1 };
+
+/* Return codes. */
+enum gg_status {
+    GG_OK = 0,            /* ready / done */
+    GG_NOT_SUPPORTED = 1, /* gg_prepare: shape or arguments refused; `why` holds the reason (N/A) */
+    GG_ERR_ARG = -1,      /* invalid call (null handle, run before prepare, ...) */
+    GG_ERR_CUDA = -2,     /* a CUDA runtime/driver call failed; see gg_last_error() */
+    GG_ERR_DEVICE = -3    /* the kernel reported a bounded-wait timeout; see gg_device_status() */
+};
+
+/* Problem descriptor: tunemax::GroupedGemmProblem (common/backend.hpp:39-60). group_m is a host
+ * array of group_num entries (any value >= 0; zero-length groups are skipped); x, w, out are
+ * device pointers owned by the caller, 16-byte aligned. Requirements checked by gg_prepare:
+ * k % 8 == 0 and n % 8 == 0 (16-byte row strides for TMA and the vector epilogue),
+ * sum(group_m) < 2^31. */
+typedef struct gg_problem {
+    int32_t dtype;          /* enum gg_dtype */
+    int32_t group_num;      /* B: number of groups (experts) */
+    int64_t n;              /* N: output columns = rows of each w[g] */
+    int64_t k;              /* K: reduction length */
+    const int64_t *group_m; /* host, [group_num] rows per group */
+    const void *x;          /* device, [sum(group_m), k] */
+    const void *w;          /* device, [group_num, n, k] */
+    void *out;              /* device, [sum(group_m), n] */
+} gg_problem;
+
+/* Create a backend instance (tunemax::make_ck_tile_backend(), common/backend.hpp:81, is the
+ * factory this one sits beside). Returns NULL only when out of host memory. */
+gg_handle *gg_create(void);
+
+/* Backend::name() (common/backend.hpp:65). Returns "b200". */
+const char *gg_name(const gg_handle *h);
+
+/* Backend::prepare() (common/backend.hpp:66; the CK version is ck_kernel/ck_grouped_gemm.cpp:
+ * 130-218). Untimed: validates the problem, builds the device group-argument buffer (per-group
+ * tile and row offsets), encodes the TMA descriptors and picks the kernel variant, then waits
+ * for `stream`. Returns GG_OK when ready, GG_NOT_SUPPORTED with a reason in `why` (if why != NULL
+ * and why_len > 0) when the shape is refused, or a negative error. */
+int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why, size_t why_len);
+
+/* Backend::run() (common/backend.hpp:67; ck_kernel/ck_grouped_gemm.cpp:140, :114-121). Timed:
+ * enqueues exactly one kernel launch on `stream` and does not synchronise. */
+int gg_run(gg_handle *h, gg_stream_t stream);
+
+/* Backend::release() (common/backend.hpp:69; ck_kernel/ck_grouped_gemm.cpp:142-146): frees
+ * what gg_prepare() allocated. The handle can be prepared again. */
+void gg_release(gg_handle *h);
+
+/* Backend::detail() (common/backend.hpp:71; ck_kernel/ck_grouped_gemm.cpp:216): kernel variant,
+ * tile shape, stages and grid of the prepared problem. Valid until the next prepare/release. */
+const char *gg_detail(const gg_handle *h);
+
+/* Message of the last failed call on this handle ("" if none). */
+const char *gg_last_error(const gg_handle *h);
+
+/* Synchronises `stream`, then reads and clears the kernel's device status word: 0 when every
+ * launch since the last read finished normally, otherwise the first bounded-wait timeout code
+ * (0x1000 | role << 8 | barrier). No counterpart in the reference, whose kernel cannot time
+ * out (its only device-side guard is a trap, ck_kernel/fast_epilogue.hpp:38-41). */
+int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
+
+/* Override the automatic choices of gg_prepare (takes effect at the next gg_prepare):
+ *   "variant"    -1 auto, 0 = 2-CTA 256x256 tile, 1 = 1-CTA 128x256, 2 = 1-CTA 128x128
+ *   "band"       M tiles per raster band (default chosen per shape), 0 = auto
+ *   "max_ctas"   cap on the persistent grid (0 = one CTA per SM)
+ *   "timeout_ms" bounded-wait limit inside the kernel (default 2000)
+ * Returns GG_OK or GG_ERR_ARG for an unknown key. The knobs are the analogue of the compile-time
+ * CkTileConfig (ck_kernel/ck_grouped_gemm_config.hpp:26-86) that the reference edits to tune. */
+int gg_set_option(gg_handle *h, const char *key, int64_t value);
+
+/* Destroy the handle (calls gg_release first). */
+void gg_destroy(gg_handle *h);
+
+/* Expert-parallel shard of `group_num` groups over `world` GPUs: contiguous ranges, the first
+ * (group_num % world) ranks get one extra group. Writes [*g0, *g1) for `rank`. Pure host
+ * arithmetic (no CUDA). The reference has no multi-GPU path; its only split of experts is the
+ * shape generator's EP divisor (scripts/gen_shapes.py:43-48). Returns GG_ERR_ARG on bad input. */
+int gg_expert_shard(int32_t group_num, int32_t world, int32_t rank, int32_t *g0, int32_t *g1);
+
+/* Library ABI version (incremented on incompatible change). */
+int gg_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GG_B200_H */

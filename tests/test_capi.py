@@ -1,0 +1,112 @@
+"""CPU tests of the C ABI (no kernel launches): symbols, host-side argument checks, expert
+sharding arithmetic and option handling. Mirrors the reference's N/A behaviour for shapes a
+backend refuses (bench/bench_main.cpp:469-472)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "gg_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gg_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol(gg):
+    lib = gg.load_library()
+    names = declared_functions()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in gg.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_abi_version_and_name(gg):
+    lib = gg.load_library()
+    assert lib.gg_abi_version() == 1
+    b = gg.B200Backend()
+    assert b.name() == "b200"
+    assert b.detail() == ""
+
+
+@pytest.mark.parametrize("g,world", [(256, 8), (256, 1), (7, 3), (3, 8), (0, 2), (33, 4)])
+def test_expert_shard_partitions_contiguously(gg, g, world):
+    ranges = [gg.expert_shard(g, world, r) for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == g
+    for (a0, a1), (b0, b1) in zip(ranges, ranges[1:]):
+        assert a1 == b0
+    sizes = [b - a for a, b in ranges]
+    assert max(sizes) - min(sizes) <= 1
+    assert sizes == sorted(sizes, reverse=True)
+
+
+def test_expert_shard_rejects_bad_args(gg):
+    with pytest.raises(gg.GGError):
+        gg.expert_shard(8, 0, 0)
+    with pytest.raises(gg.GGError):
+        gg.expert_shard(8, 2, 2)
+
+
+def test_set_option(gg):
+    b = gg.B200Backend()
+    b.set_option("variant", 1)
+    b.set_option("band", 4)
+    b.set_option("timeout_ms", 500)
+    b.set_option("max_ctas", 64)
+    for key, val in (("variant", 7), ("band", -1), ("timeout_ms", 0), ("bogus", 1)):
+        with pytest.raises(gg.GGError):
+            b.set_option(key, val)
+
+
+ALIGNED = 0x10000
+
+
+@pytest.mark.parametrize(
+    "kw,reason",
+    [
+        (dict(dtype=5), "dtype"),
+        (dict(group_m=[]), "group_num"),
+        (dict(group_m=[4, -1]), "group_m"),
+        (dict(k=100), "k must be a multiple of 8"),
+        (dict(n=1000 + 4), "n must be a multiple of 8"),
+        (dict(n=0), "n and k"),
+        (dict(x=ALIGNED + 8), "16-byte aligned"),
+        (dict(out=0), "non-null"),
+        (dict(group_m=[1 << 30, 1 << 30]), "2^31"),
+    ],
+)
+def test_prepare_refuses_unsupported_shapes(gg, kw, reason):
+    args = dict(dtype=gg.BF16, group_m=[4, 4], n=64, k=64, x=ALIGNED, w=ALIGNED, out=ALIGNED)
+    args.update(kw)
+    b = gg.B200Backend()
+    why = b.prepare(args["dtype"], args["group_m"], args["n"], args["k"], args["x"], args["w"], args["out"])
+    assert reason in why
+    with pytest.raises(gg.GGError):
+        b.run()  # not prepared
+
+
+def test_prepare_without_gpu_fails_loudly(gg):
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    b = gg.B200Backend()
+    with pytest.raises(gg.GGError) as e:
+        b.prepare(gg.BF16, [4], 64, 64, ALIGNED, ALIGNED, ALIGNED)
+    assert e.value.code == gg.GG_ERR_CUDA
+
+
+def test_null_handle_is_rejected(gg):
+    lib = gg.load_library()
+    assert lib.gg_run(None, None) == gg.GG_ERR_ARG
+    assert lib.gg_prepare(None, None, None, None, 0) == gg.GG_ERR_ARG
+    st = ctypes.c_uint32(0)
+    assert lib.gg_device_status(None, None, ctypes.byref(st)) == gg.GG_ERR_ARG
+    lib.gg_release(None)
+    lib.gg_destroy(None)
