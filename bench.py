@@ -142,27 +142,25 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def cpu_baseline(cfg, budget_s: float = 10.0):
-    """Oracle port of the fp32 reference path on all host cores, on a bounded sample: the first
-    R rows of one expert against its full weight (2*R*N*K flop), R sized for ~budget_s."""
+def cpu_baseline(cfg, budget_s: float = 20.0):
+    """Oracle port of the fp32 reference path on all host cores. Whole experts of the workload
+    (M x N x K each) are computed one after another until every expert of one GPU's share is
+    done or `budget_s` has passed; the sample is the experts completed."""
     orc = load_oracle()
     dt = 0 if cfg["dtype"] == "bf16" else 1
-    n, k = cfg["n"], cfg["k"]
+    n, k, m, b = cfg["n"], cfg["k"], cfg["m"], cfg["b"]
     threads = orc.hw_threads()
-    m = cfg["m"]
-    x, w = orc.make_inputs([m], n, k, dt)
-    probe = 16
-    t0 = time.perf_counter()
-    orc.grouped_gemm_f32(x, w, [m], dt, max_rows=probe, threads=threads)
-    dt_probe = time.perf_counter() - t0
-    rows = int(max(16, min(m, probe * budget_s / max(dt_probe, 1e-6))))
-    rows = rows // 16 * 16 or 16
-    t0 = time.perf_counter()
-    orc.grouped_gemm_f32(x, w, [m], dt, max_rows=rows, threads=threads)
-    el = time.perf_counter() - t0
-    flops = 2.0 * rows * n * k
+    x, w = orc.make_inputs([m], n, k, dt)  # one expert's operands, reused per expert
+    done, el = 0, 0.0
+    out = np.zeros((m, n), np.float32)
+    while done < b and el < budget_s:
+        t0 = time.perf_counter()
+        orc.grouped_gemm_f32(x, w, [m], dt, threads=threads, out=out)
+        el += time.perf_counter() - t0
+        done += 1
+    flops = 2.0 * done * m * n * k
     return {"value": round(flops / el / 1e12, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
-            "sample": f"fp32 GEMM of {rows} rows x N={n} x K={k} of one expert ({flops / 1e9:.1f} GFLOP, "
+            "sample": f"{done} of {b} experts of the workload (each fp32 {m}x{n}x{k}; {flops / 1e9:.0f} GFLOP, "
                       f"{el:.2f} s) with the oracle port on {threads} host threads"}
 
 

@@ -117,17 +117,31 @@ inline uint64_t splitmix64(uint64_t x) {
     return x ^ (x >> 31);
 }
 
-// One standard-normal value for element i (bench/bench_main.cpp:171-174). The uniform
-// variates are formed exactly as the reference forms them (in float). The transcendental
-// part uses host libm in double precision, rounded to float: the reference uses the device
-// logf / cospif, so a value can differ from the reference's by an ulp of float, and very
-// rarely its 16-bit rounding by one ulp (the golden test measures how often).
+// One standard-normal value for element i (bench/bench_main.cpp:171-174), with the same
+// sequence of float operations as the reference: u1, u2 in float; log(u1) rounded to float;
+// times -2 (exact); square root rounded to float; cos(pi * 2*u2) rounded to float; product
+// rounded to float. The two transcendental steps are evaluated in double precision and
+// rounded once (correctly rounded in practice); the reference uses the device logf / cospif,
+// which may differ by an ulp of float, so very rarely the 16-bit rounding of a value differs
+// by one ulp (the golden test bounds how often).
+// cos(pi * x) for x in [0, 2], in double, with an exact argument reduction so the result keeps
+// full relative precision near the zeros of cos (x = 0.5, 1.5).
+inline double cospi_0_2(double x) {
+    double y = x > 1.0 ? 2.0 - x : x;  // cos(pi (2 - y)) = cos(pi y); exact
+    if (y <= 0.25)
+        return std::cos(M_PI * y);
+    if (y <= 0.75)
+        return std::sin(M_PI * (0.5 - y));  // 0.5 - y exact
+    return -std::cos(M_PI * (1.0 - y));     // 1 - y exact
+}
+
 inline float randn_at(uint64_t seed, uint64_t i) {
     const uint64_t r = splitmix64(seed ^ (i * 0x2545F4914F6CDD1Dull));
     const float u1 = (float(r >> 40) + 1.0f) * (1.0f / 16777217.0f);
     const float u2 = float((r >> 16) & 0xFFFFFF) * (1.0f / 16777216.0f);
-    const float mag = float(std::sqrt(-2.0 * std::log(double(u1))));
-    const float ang = float(std::cos(M_PI * double(2.0f * u2)));
+    const float lg = float(std::log(double(u1)));
+    const float mag = std::sqrt(-2.0f * lg);
+    const float ang = float(cospi_0_2(double(2.0f * u2)));
     return mag * ang;
 }
 
