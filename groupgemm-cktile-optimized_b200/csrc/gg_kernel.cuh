@@ -129,15 +129,15 @@ struct Abort {
     uint64_t timeout_ns;
 };
 
-// Bounded wait by one lane. Returns false if this or another role gave up.
-__device__ __noinline__ bool wait_lane(uint32_t bar, uint32_t parity, const Abort &ab, uint32_t code) {
-    if (ptx::mbar_try_wait(bar, parity))
-        return true;
+// Slow path of a bounded wait: spin on try_wait, and every 256 tries check the abort flags
+// and the time limit. Returns false if this or another role gave up.
+template <bool kClusterScope>
+__device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, const Abort ab, uint32_t code) {
     const uint64_t t0 = ptx::globaltimer();
     for (uint32_t it = 1;; ++it) {
-        if (ptx::mbar_try_wait(bar, parity))
+        if (kClusterScope ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity))
             return true;
-        if ((it & 31u) == 0) {
+        if ((it & 255u) == 0) {
             if (*ab.flag != 0u || *(volatile uint32_t *)ab.status != 0u) {
                 *ab.flag = 1u;
                 return false;
@@ -151,11 +151,19 @@ __device__ __noinline__ bool wait_lane(uint32_t bar, uint32_t parity, const Abor
     }
 }
 
+// Bounded wait by one thread: an inline first test, the loop out of line.
+template <bool kClusterScope = false>
+__device__ __forceinline__ bool wait_one(uint32_t bar, uint32_t parity, const Abort &ab, uint32_t code) {
+    if (kClusterScope ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity))
+        return true;
+    return wait_slow<kClusterScope>(bar, parity, ab, code);
+}
+
 // Warp-uniform bounded wait: lane 0 waits, the result is broadcast.
 __device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, const Abort &ab, uint32_t code) {
     int ok = 1;
-    if (ptx::lane_id() == 0)
-        ok = wait_lane(bar, parity, ab, code) ? 1 : 0;
+    if ((threadIdx.x & 31u) == 0)
+        ok = wait_one(bar, parity, ab, code) ? 1 : 0;
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
@@ -190,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile uint32_t *abort_flag = tmem_ptr_slot + 1;
 
     const int warp = threadIdx.x / 32;
-    const uint32_t lane = threadIdx.x % 32;
+    const uint32_t lane = threadIdx.x & 31u;
     const uint32_t cta_rank = kCG == 2 ? ptx::cluster_ctarank() : 0u;
     const bool leader = cta_rank == 0;
     const int cluster_id = blockIdx.x / kCG;
@@ -227,23 +235,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     const Abort ab{p.status, abort_flag, p.timeout_ns};
 
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
-        const uint32_t full_leader0 = kCG == 2 ? ptx::mapa(full_bar(0), 0) : full_bar(0);
-        int cursor = 0;
-        uint32_t it = 0;
-        bool ok = true;
-        for (int t = cluster_id; t < p.total_tiles && ok; t += num_clusters) {
-            const TileCoord tc = decode_tile<C::kClusterM>(p, t, cursor);
-            const int a_row = __ldg(&p.row_off[tc.g]) + tc.mt * C::kClusterM + int(cta_rank) * kBM;
-            const int b_row = tc.nt * kBN + int(cta_rank) * C::kBRows;
-            for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
-                const int s = int(it % C::kStages);
-                const uint32_t ph = (it / C::kStages) & 1u;
-                if (!wait_warp(empty_bar(s), ph ^ 1u, ab, kStatusTimeout | kRoleProducer | uint32_t(s))) {
-                    ok = false;
-                    break;
-                }
-                if (lane == 0) {
+        // ---------------- TMA producer (one thread) ----------------
+        if (lane == 0) {
+            const uint32_t full_leader0 = kCG == 2 ? ptx::mapa(full_bar(0), 0) : full_bar(0);
+            int cursor = 0;
+            uint32_t it = 0;
+            bool ok = true;
+            for (int t = cluster_id; t < p.total_tiles && ok; t += num_clusters) {
+                const TileCoord tc = decode_tile<C::kClusterM>(p, t, cursor);
+                const int a_row = __ldg(&p.row_off[tc.g]) + tc.mt * C::kClusterM + int(cta_rank) * kBM;
+                const int b_row = tc.nt * kBN + int(cta_rank) * C::kBRows;
+                for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+                    const int s = int(it % C::kStages);
+                    const uint32_t ph = (it / C::kStages) & 1u;
+                    if (!wait_one(empty_bar(s), ph ^ 1u, ab, kStatusTimeout | kRoleProducer | uint32_t(s))) {
+                        ok = false;
+                        break;
+                    }
                     const uint32_t a_dst = smem_base + uint32_t(s) * C::kStageBytes;
                     const uint32_t b_dst = a_dst + C::kABytes;
                     const uint32_t fb = full_leader0 + 8u * s;
@@ -257,16 +265,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ptx::tma_load_3d_pair(b_dst, &tmap_b, fb, kb * kBK, b_row, tc.g);
                     }
                 }
-                __syncwarp();
             }
+            // Tail: every stage released, so no tcgen05.commit is still in flight to this CTA.
+            for (uint32_t i = it; ok && i < it + C::kStages; ++i)
+                ok = wait_one(empty_bar(int(i % C::kStages)), ((i / C::kStages) & 1u) ^ 1u, ab,
+                              kStatusTimeout | kRoleProducer | 0x80u);
         }
-        // Tail: every stage released, so no tcgen05.commit is still in flight to this CTA.
-        for (uint32_t i = it; ok && i < it + C::kStages; ++i)
-            ok = wait_warp(empty_bar(int(i % C::kStages)), ((i / C::kStages) & 1u) ^ 1u, ab,
-                           kStatusTimeout | kRoleProducer | 0x80u);
+        __syncwarp();
     } else if (warp == 1) {
-        // ---------------- MMA issuer (pair leader only) ----------------
-        if (leader) {
+        // ---------------- MMA issuer (one thread of the pair leader) ----------------
+        if (leader && lane == 0) {
             int cursor = 0;
             uint32_t it = 0, tl = 0;
             bool ok = true;
@@ -274,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 (void)decode_tile<C::kClusterM>(p, t, cursor);
                 const int acc = int(tl & 1u);
                 const uint32_t acc_ph = (tl >> 1) & 1u;
-                if (!wait_warp(tempty_bar(acc), acc_ph ^ 1u, ab, kStatusTimeout | kRoleMma | 0x40u | uint32_t(acc))) {
+                if (!wait_one<true>(tempty_bar(acc), acc_ph ^ 1u, ab, kStatusTimeout | kRoleMma | 0x40u | uint32_t(acc))) {
                     ok = false;
                     break;
                 }
@@ -283,41 +291,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
                     const int s = int(it % C::kStages);
                     const uint32_t ph = (it / C::kStages) & 1u;
-                    if (!wait_warp(full_bar(s), ph, ab, kStatusTimeout | kRoleMma | uint32_t(s))) {
+                    if (!wait_one(full_bar(s), ph, ab, kStatusTimeout | kRoleMma | uint32_t(s))) {
                         ok = false;
                         break;
                     }
                     ptx::tc_fence_after();
-                    if (lane == 0) {
-                        const uint32_t a_addr = smem_base + uint32_t(s) * C::kStageBytes;
-                        const uint32_t b_addr = a_addr + C::kABytes;
-                        const uint64_t adesc = ptx::sw128_kmajor_desc(a_addr);
-                        const uint64_t bdesc = ptx::sw128_kmajor_desc(b_addr);
+                    const uint32_t a_addr = smem_base + uint32_t(s) * C::kStageBytes;
+                    const uint32_t b_addr = a_addr + C::kABytes;
+                    const uint64_t adesc = ptx::sw128_kmajor_desc(a_addr);
+                    const uint64_t bdesc = ptx::sw128_kmajor_desc(b_addr);
 #pragma unroll
-                        for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-                            // advance 16 elements (32 bytes) along K inside the swizzle atom
-                            ptx::umma_f16<kCG>(d_tmem, adesc + uint64_t(kk * 2), bdesc + uint64_t(kk * 2), kIdesc,
-                                               (kb | kk) != 0 ? 1u : 0u);
-                        }
-                        ptx::umma_commit<kCG>(empty_bar(s));
-                        if constexpr (kCG == 2)
-                            ptx::umma_commit<kCG>(ptx::mapa(empty_bar(s), 1));
+                    for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+                        // advance 16 elements (32 bytes) along K inside the swizzle atom
+                        ptx::umma_f16<kCG>(d_tmem, adesc + uint64_t(kk * 2), bdesc + uint64_t(kk * 2), kIdesc,
+                                           (kb | kk) != 0 ? 1u : 0u);
                     }
-                    __syncwarp();
+                    ptx::umma_commit<kCG>(empty_bar(s));
+                    if constexpr (kCG == 2)
+                        ptx::umma_commit<kCG>(ptx::mapa(empty_bar(s), 1));
                 }
                 if (!ok)
                     break;
-                if (lane == 0) {
-                    ptx::umma_commit<kCG>(tfull_bar(acc));
-                    if constexpr (kCG == 2)
-                        ptx::umma_commit<kCG>(ptx::mapa(tfull_bar(acc), 1));
-                }
-                __syncwarp();
+                ptx::umma_commit<kCG>(tfull_bar(acc));
+                if constexpr (kCG == 2)
+                    ptx::umma_commit<kCG>(ptx::mapa(tfull_bar(acc), 1));
             }
             // Tail: both accumulators released by every epilogue warp of the pair.
             for (uint32_t i = tl; ok && i < tl + 2; ++i)
-                ok = wait_warp(tempty_bar(int(i & 1u)), ((i >> 1) & 1u) ^ 1u, ab, kStatusTimeout | kRoleMma | 0x80u);
+                ok = wait_one<true>(tempty_bar(int(i & 1u)), ((i >> 1) & 1u) ^ 1u, ab,
+                                    kStatusTimeout | kRoleMma | 0x80u);
         }
+        __syncwarp();
     } else {
         // ---------------- epilogue (4 warps) ----------------
         const int q = warp & 3;  // TMEM lane quarter this warp may access
