@@ -19,6 +19,16 @@
 #include "gg_b200.h"
 #include "gg_kernel.cuh"
 
+#ifndef GG_ATOMS_V0
+#define GG_ATOMS_V0 2
+#endif
+#ifndef GG_ATOMS_V1
+#define GG_ATOMS_V1 1
+#endif
+#ifndef GG_ATOMS_V2
+#define GG_ATOMS_V2 2
+#endif
+
 namespace {
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -47,21 +57,24 @@ struct Variant {
     int smem;
     const void *fn_bf16;
     const void *fn_fp16;
+    int atoms;     // 64-element K atoms per stage
 };
 
-template <int kCG, int kBN> Variant make_variant() {
-    using C = gg::TileCfg<kCG, kBN>;
+template <int kCG, int kBN, int kAtoms> Variant make_variant() {
+    using C = gg::TileCfg<kCG, kBN, kAtoms>;
     return Variant{kCG,
                    kBN,
                    C::kClusterM,
                    C::kStages,
                    C::kSmemBytes,
-                   reinterpret_cast<const void *>(&gg::grouped_gemm_sm100<__nv_bfloat16, kCG, kBN>),
-                   reinterpret_cast<const void *>(&gg::grouped_gemm_sm100<__half, kCG, kBN>)};
+                   reinterpret_cast<const void *>(&gg::grouped_gemm_sm100<__nv_bfloat16, kCG, kBN, kAtoms>),
+                   reinterpret_cast<const void *>(&gg::grouped_gemm_sm100<__half, kCG, kBN, kAtoms>),
+                   kAtoms};
 }
 
 const Variant &variant_at(int i) {
-    static const Variant v[3] = {make_variant<2, 256>(), make_variant<1, 256>(), make_variant<1, 128>()};
+    static const Variant v[3] = {make_variant<2, 256, GG_ATOMS_V0>(), make_variant<1, 256, GG_ATOMS_V1>(),
+                                 make_variant<1, 128, GG_ATOMS_V2>()};
     return v[i];
 }
 constexpr int kNumVariants = 3;
@@ -130,16 +143,22 @@ int64_t tiles_for(const gg_problem *p, const Variant &v) {
     return t;
 }
 
-// Automatic variant choice: the largest tile that still gives every SM (pair) work; smaller
-// tiles only for low-tile-count shapes (the reference loses there, README.md:56-58).
+// Automatic variant choice (measured on B200: the 256x256 pair tile has the highest rate per SM,
+// then 128x256, then 128x128, but small problems are bound by one tile's latency):
+//   1. the whole problem fits in one wave of 128x128 tiles -> 128x128 (least work per CTA);
+//   2. at least one full wave of 256x256 pair tiles        -> 256x256;
+//   3. one wave of 128x256 tiles                           -> 128x256 (as many SMs, half the
+//                                                             work per SM of a pair tile);
+//   4. otherwise                                           -> 256x256.
+// Low-tile-count shapes are where the reference loses to hipBLASLt (README.md:56-58).
 int choose_variant(const gg_problem *p, int num_sms) {
-    const int64_t t0 = tiles_for(p, variant_at(0));
-    if (t0 >= int64_t(num_sms / 2) * 3 / 4)
+    if (tiles_for(p, variant_at(2)) <= num_sms)
+        return 2;
+    if (tiles_for(p, variant_at(0)) >= num_sms / 2)
         return 0;
-    const int64_t t1 = tiles_for(p, variant_at(1));
-    if (t1 >= int64_t(num_sms) * 3 / 4)
+    if (tiles_for(p, variant_at(1)) <= num_sms)
         return 1;
-    return 2;
+    return 0;
 }
 
 }  // namespace
@@ -380,7 +399,7 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     h->cg = v.cg;
     char d[256];
     std::snprintf(d, sizeof(d), "gg_sm100<%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld grid=%d band=%d",
-                  p->dtype == GG_BF16 ? "bf16" : "fp16", v.cluster_m, v.bn, gg::kBK, v.cg, v.stages,
+                  p->dtype == GG_BF16 ? "bf16" : "fp16", v.cluster_m, v.bn, gg::kBK * v.atoms, v.cg, v.stages,
                   (long long)tiles, h->grid, band);
     h->detail = d;
     h->ready = true;

@@ -44,7 +44,7 @@ namespace gg {
 
 constexpr int kThreads = 192;  // 6 warps: producer, MMA, 4 x epilogue
 constexpr int kBM = 128;       // accumulator rows per CTA (TMEM lanes)
-constexpr int kBK = 64;        // K per stage: one 128-byte swizzle row of 16-bit elements
+constexpr int kBK = 64;        // K per swizzle atom: one 128-byte row of 16-bit elements
 constexpr int kUmmaK = 16;     // K per tcgen05.mma (kind::f16)
 constexpr int kSmemBudget = 200 * 1024;
 
@@ -64,7 +64,7 @@ struct KernelParams {
     int32_t group_num;
     int32_t n;
     int32_t k;
-    int32_t num_kb;       // ceil(K / 64)
+    int32_t num_kb;       // ceil(K / 64): K atoms
     int32_t tiles_n;      // ceil(N / BN)
     int32_t total_tiles;  // tile_off[G]
     int32_t band;         // M tiles per raster band (L2 reuse of the weight panel)
@@ -80,13 +80,18 @@ template <> struct Fmt<__half> {
     static constexpr uint32_t kUmma = 0;
 };
 
-template <int kCG, int kBN> struct TileCfg {
+// A stage holds kAtoms K-atoms (64 elements each) of the A and B tiles, so one barrier wait and
+// one commit of the MMA thread cover kAtoms x 4 tcgen05.mma instructions.
+template <int kCG, int kBN, int kAtoms> struct TileCfg {
     static_assert(kCG == 1 || kCG == 2, "CTA group of 1 or 2");
     static_assert(kBN % 16 == 0 && kBN >= 32 && kBN <= 256, "UMMA N");
+    static_assert(kAtoms >= 1 && kAtoms <= 4, "atoms per stage");
     static constexpr int kClusterM = kBM * kCG;  // rows per (cluster) tile
     static constexpr int kBRows = kBN / kCG;     // weight rows each CTA loads
-    static constexpr int kABytes = kBM * kBK * 2;
-    static constexpr int kBBytes = kBRows * kBK * 2;
+    static constexpr int kAAtomBytes = kBM * kBK * 2;
+    static constexpr int kBAtomBytes = kBRows * kBK * 2;
+    static constexpr int kABytes = kAtoms * kAAtomBytes;
+    static constexpr int kBBytes = kAtoms * kBAtomBytes;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
     static constexpr int kTmemCols = (2 * kBN) <= 32 ? 32 : (2 * kBN) <= 64 ? 64 : (2 * kBN) <= 128 ? 128
@@ -95,6 +100,7 @@ template <int kCG, int kBN> struct TileCfg {
     static constexpr int kBarOffset = kStages * kStageBytes;
     static constexpr int kSmemBytes = kBarOffset + (2 * kStages + 4) * 8 + 16 + 1024;  // + align slack
     static_assert(kStages >= 2, "ring too shallow");
+    static_assert(kAAtomBytes % 1024 == 0 && kBAtomBytes % 1024 == 0, "swizzle atoms 1024-byte aligned");
 };
 
 struct TileCoord {
@@ -178,11 +184,11 @@ __device__ __forceinline__ uint32_t pack2(uint32_t a, uint32_t b) {
     }
 }
 
-template <typename T, int kCG, int kBN>
+template <typename T, int kCG, int kBN, int kAtoms>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_sm100(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                        const __grid_constant__ KernelParams p) {
-    using C = TileCfg<kCG, kBN>;
+    using C = TileCfg<kCG, kBN, kAtoms>;
     constexpr uint32_t kIdesc = ptx::f16_idesc(Fmt<T>::kUmma, kBM * kCG, kBN);
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -233,50 +239,68 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_ptr_slot;
 
     const Abort ab{p.status, abort_flag, p.timeout_ns};
+    const int num_ks = (p.num_kb + kAtoms - 1) / kAtoms;  // stages per tile
 
     if (warp == 0) {
         // ---------------- TMA producer (one thread) ----------------
         if (lane == 0) {
             const uint32_t full_leader0 = kCG == 2 ? ptx::mapa(full_bar(0), 0) : full_bar(0);
             int cursor = 0;
-            uint32_t it = 0;
+            int s = 0;
+            uint32_t ph = 0;
             bool ok = true;
             for (int t = cluster_id; t < p.total_tiles && ok; t += num_clusters) {
                 const TileCoord tc = decode_tile<C::kClusterM>(p, t, cursor);
                 const int a_row = __ldg(&p.row_off[tc.g]) + tc.mt * C::kClusterM + int(cta_rank) * kBM;
                 const int b_row = tc.nt * kBN + int(cta_rank) * C::kBRows;
-                for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
-                    const int s = int(it % C::kStages);
-                    const uint32_t ph = (it / C::kStages) & 1u;
+                for (int ks = 0; ks < num_ks; ++ks) {
                     if (!wait_one(empty_bar(s), ph ^ 1u, ab, kStatusTimeout | kRoleProducer | uint32_t(s))) {
                         ok = false;
                         break;
                     }
+                    // K atoms of this stage that lie inside K (the rest would be all zero fill)
+                    const int na = min(kAtoms, p.num_kb - ks * kAtoms);
                     const uint32_t a_dst = smem_base + uint32_t(s) * C::kStageBytes;
                     const uint32_t b_dst = a_dst + C::kABytes;
                     const uint32_t fb = full_leader0 + 8u * s;
                     if (leader)
-                        ptx::mbar_arrive_expect_tx(full_bar(s), uint32_t(kCG * C::kStageBytes));
-                    if constexpr (kCG == 1) {
-                        ptx::tma_load_2d(a_dst, &tmap_a, fb, kb * kBK, a_row);
-                        ptx::tma_load_3d(b_dst, &tmap_b, fb, kb * kBK, b_row, tc.g);
-                    } else {
-                        ptx::tma_load_2d_pair(a_dst, &tmap_a, fb, kb * kBK, a_row);
-                        ptx::tma_load_3d_pair(b_dst, &tmap_b, fb, kb * kBK, b_row, tc.g);
+                        ptx::mbar_arrive_expect_tx(full_bar(s), uint32_t(kCG * na * (C::kAAtomBytes + C::kBAtomBytes)));
+#pragma unroll
+                    for (int a = 0; a < kAtoms; ++a) {
+                        if (a < na) {
+                            const int k0 = (ks * kAtoms + a) * kBK;
+                            if constexpr (kCG == 1) {
+                                ptx::tma_load_2d(a_dst + a * C::kAAtomBytes, &tmap_a, fb, k0, a_row);
+                                ptx::tma_load_3d(b_dst + a * C::kBAtomBytes, &tmap_b, fb, k0, b_row, tc.g);
+                            } else {
+                                ptx::tma_load_2d_pair(a_dst + a * C::kAAtomBytes, &tmap_a, fb, k0, a_row);
+                                ptx::tma_load_3d_pair(b_dst + a * C::kBAtomBytes, &tmap_b, fb, k0, b_row, tc.g);
+                            }
+                        }
+                    }
+                    if (++s == C::kStages) {
+                        s = 0;
+                        ph ^= 1u;
                     }
                 }
             }
             // Tail: every stage released, so no tcgen05.commit is still in flight to this CTA.
-            for (uint32_t i = it; ok && i < it + C::kStages; ++i)
-                ok = wait_one(empty_bar(int(i % C::kStages)), ((i / C::kStages) & 1u) ^ 1u, ab,
-                              kStatusTimeout | kRoleProducer | 0x80u);
+            for (int i = 0; ok && i < C::kStages; ++i) {
+                ok = wait_one(empty_bar(s), ph ^ 1u, ab, kStatusTimeout | kRoleProducer | 0x80u);
+                if (++s == C::kStages) {
+                    s = 0;
+                    ph ^= 1u;
+                }
+            }
         }
         __syncwarp();
     } else if (warp == 1) {
         // ---------------- MMA issuer (one thread of the pair leader) ----------------
         if (leader && lane == 0) {
             int cursor = 0;
-            uint32_t it = 0, tl = 0;
+            uint32_t tl = 0;
+            int s = 0;
+            uint32_t ph = 0;
             bool ok = true;
             for (int t = cluster_id; t < p.total_tiles && ok; t += num_clusters, ++tl) {
                 (void)decode_tile<C::kClusterM>(p, t, cursor);
@@ -288,27 +312,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 ptx::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + uint32_t(acc * kBN);
-                for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
-                    const int s = int(it % C::kStages);
-                    const uint32_t ph = (it / C::kStages) & 1u;
+                for (int ks = 0; ks < num_ks; ++ks) {
                     if (!wait_one(full_bar(s), ph, ab, kStatusTimeout | kRoleMma | uint32_t(s))) {
                         ok = false;
                         break;
                     }
                     ptx::tc_fence_after();
+                    const int na = min(kAtoms, p.num_kb - ks * kAtoms);
                     const uint32_t a_addr = smem_base + uint32_t(s) * C::kStageBytes;
-                    const uint32_t b_addr = a_addr + C::kABytes;
                     const uint64_t adesc = ptx::sw128_kmajor_desc(a_addr);
-                    const uint64_t bdesc = ptx::sw128_kmajor_desc(b_addr);
+                    const uint64_t bdesc = ptx::sw128_kmajor_desc(a_addr + C::kABytes);
 #pragma unroll
-                    for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-                        // advance 16 elements (32 bytes) along K inside the swizzle atom
-                        ptx::umma_f16<kCG>(d_tmem, adesc + uint64_t(kk * 2), bdesc + uint64_t(kk * 2), kIdesc,
-                                           (kb | kk) != 0 ? 1u : 0u);
+                    for (int a = 0; a < kAtoms; ++a) {
+                        if (a < na) {
+#pragma unroll
+                            for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+                                // atom a, then 16 elements (32 bytes) along K inside the swizzle atom
+                                const uint64_t da = uint64_t((a * C::kAAtomBytes + kk * 32) >> 4);
+                                const uint64_t db = uint64_t((a * C::kBAtomBytes + kk * 32) >> 4);
+                                ptx::umma_f16<kCG>(d_tmem, adesc + da, bdesc + db, kIdesc,
+                                                   (ks | a | kk) != 0 ? 1u : 0u);
+                            }
+                        }
                     }
                     ptx::umma_commit<kCG>(empty_bar(s));
                     if constexpr (kCG == 2)
                         ptx::umma_commit<kCG>(ptx::mapa(empty_bar(s), 1));
+                    if (++s == C::kStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
                 }
                 if (!ok)
                     break;
