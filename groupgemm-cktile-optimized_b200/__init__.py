@@ -56,6 +56,8 @@ SIGNATURES = {
     "gg_destroy": (None, [ctypes.c_void_p]),
     "gg_expert_shard": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                        ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]),
+    "gg_run_noalloc": (ctypes.c_int, [ctypes.POINTER(GGProblem), ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32),
+                                      ctypes.c_char_p, ctypes.c_size_t]),
 }
 
 _lib = None
@@ -155,6 +157,25 @@ class B200Backend:
         if rc not in (GG_OK, GG_ERR_DEVICE):
             raise GGError(rc, self.last_error())
         return st.value
+
+
+def run_noalloc(dtype: int, group_m: Sequence[int], n: int, k: int, x_ptr: int, w_ptr: int, out_ptr: int,
+                stream: int = 0, wait: bool = False) -> tuple[int, str, int]:
+    """gg_run_noalloc: one grouped GEMM for callers that cannot allocate device memory.
+
+    The library keeps its small per-call scratch (group offsets and status word, at most 1024
+    groups) in a fixed device array instead of allocating it, so nothing is allocated here.
+    Returns (return code, reason or error text, kernel status when `wait`, else 0). Calls that
+    can overlap on the GPU share that array and race; calls in order on one stream are fine."""
+    lib = load_library()
+    gm = (ctypes.c_int64 * len(group_m))(*[int(m) for m in group_m])
+    prob = GGProblem(int(dtype), len(group_m), int(n), int(k), gm, ctypes.c_void_p(x_ptr or None),
+                     ctypes.c_void_p(w_ptr or None), ctypes.c_void_p(out_ptr or None))
+    why = ctypes.create_string_buffer(256)
+    st = ctypes.c_uint32(0)
+    rc = lib.gg_run_noalloc(ctypes.byref(prob), ctypes.c_void_p(stream or None),
+                            ctypes.byref(st) if wait else None, why, 256)
+    return rc, why.value.decode(), st.value
 
 
 def make_b200_backend() -> B200Backend:

@@ -12,6 +12,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -445,3 +446,274 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Entry point that allocates nothing: gg_run_noalloc.
+//
+// Some callers cannot allocate device memory at the moment they want the GEMM: an inference
+// engine that has reserved (nearly) all HBM up front for weights and KV cache through its own
+// pool and fails any allocation outside it; a plugin host that hands out a fixed memory budget;
+// a latency-critical path where cudaMalloc/cudaFree are off limits because they can synchronise
+// the device. gg_prepare() allocates two small device buffers per handle (the per-group tile and
+// row offsets, and the kernel's status word), so those callers cannot use it.
+//
+// gg_run_noalloc keeps that scratch instead in one file-scope device array, g_noalloc_scratch,
+// sized for at most kNoAllocMaxGroups groups (about 8 KB). It is part of the library image, so
+// every GPU that loads the library holds it until the process exits. The caller still passes x,
+// w and out; the library allocates nothing, neither device nor host memory on the heap.
+// ---------------------------------------------------------------------------------------------
+namespace {
+
+constexpr int kNoAllocMaxGroups = 1024;
+constexpr size_t kNoAllocHeader = 256;  // status word, padded to keep the offsets 256-aligned
+constexpr size_t kNoAllocScratchBytes = kNoAllocHeader + 2 * (kNoAllocMaxGroups + 1) * sizeof(int32_t);
+
+// Device-side scratch shared by every gg_run_noalloc call on a device. In host code this name
+// is only a stand-in for the symbol, never a device address: the address comes from
+// cudaGetSymbolAddress (see noalloc_device_setup).
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+
+struct NoAllocDevice {
+    bool ready = false;
+    unsigned char *scratch = nullptr;  // device address of g_noalloc_scratch on this device
+    int num_sms = 0;
+    int clusters_v0 = 0;  // co-resident CTA pairs of the 256x256 variant (any dtype)
+};
+
+std::mutex g_noalloc_mutex;
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+
+void copy_msg(char *why, size_t why_len, const char *msg) {
+    if (why && why_len > 0) {
+        std::strncpy(why, msg, why_len - 1);
+        why[why_len - 1] = '\0';
+    }
+}
+
+// One-time set-up of device `dev` (the current device): the scratch address, the SM count, the
+// dynamic shared-memory limit of every kernel variant and the pair occupancy of the 2-CTA one.
+cudaError_t noalloc_device_setup(int dev, NoAllocDevice &d) {
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void **>(&d.scratch), g_noalloc_scratch);
+    if (e != cudaSuccess)
+        return e;
+    if ((e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return e;
+    for (int i = 0; i < kNumVariants; ++i) {
+        const Variant &v = variant_at(i);
+        for (const void *fn : {v.fn_bf16, v.fn_fp16})
+            if ((e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem)) != cudaSuccess)
+                return e;
+    }
+    const Variant &v0 = variant_at(0);
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(unsigned(d.num_sms), 1, 1);
+    cfg.blockDim = dim3(gg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = size_t(v0.smem);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if ((e = cudaOccupancyMaxActiveClusters(&d.clusters_v0, v0.fn_bf16, &cfg)) != cudaSuccess)
+        return e;
+    d.ready = true;
+    return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t *status_out, char *why,
+                              size_t why_len) {
+    if (why && why_len)
+        why[0] = '\0';
+    if (status_out)
+        *status_out = 0;
+    if (!p) {
+        copy_msg(why, why_len, "null problem");
+        return GG_ERR_ARG;
+    }
+    // ---- the same shape rules as gg_prepare, plus the scratch limit ----
+    const char *bad = nullptr;
+    if (p->dtype != GG_BF16 && p->dtype != GG_FP16)
+        bad = "dtype must be bf16 (0) or fp16 (1)";
+    else if (p->group_num < 1)
+        bad = "group_num must be >= 1";
+    else if (p->group_num > kNoAllocMaxGroups)
+        bad = "group_num exceeds the 1024 groups that gg_run_noalloc's fixed scratch holds";
+    else if (!p->group_m)
+        bad = "group_m is null";
+    else if (p->n < 1 || p->k < 1)
+        bad = "n and k must be >= 1";
+    else if (p->k % 8 != 0)
+        bad = "k must be a multiple of 8 (16-byte TMA row stride)";
+    else if (p->n % 8 != 0)
+        bad = "n must be a multiple of 8 (16-byte output row stride)";
+    else if (p->n > (int64_t(1) << 30) || p->k > (int64_t(1) << 30))
+        bad = "n and k must be below 2^30";
+    else if (int64_t(p->group_num) * p->n * p->k >= (int64_t(1) << 40) / 2)
+        bad = "weight tensor too large for one TMA descriptor";
+    int64_t total_m = 0;
+    for (int g = 0; !bad && g < p->group_num; ++g) {
+        if (p->group_m[g] < 0)
+            bad = "group_m entries must be >= 0";
+        total_m += p->group_m[g];
+        if (total_m >= (int64_t(1) << 31))
+            bad = "sum(group_m) must be below 2^31";
+    }
+    if (!bad && total_m > 0 && (!p->x || !p->w || !p->out))
+        bad = "x, w and out must be non-null device pointers";
+    if (!bad && ((reinterpret_cast<uintptr_t>(p->x) | reinterpret_cast<uintptr_t>(p->w) |
+                  reinterpret_cast<uintptr_t>(p->out)) & 15u))
+        bad = "x, w and out must be 16-byte aligned";
+    if (bad) {
+        copy_msg(why, why_len, bad);
+        return GG_NOT_SUPPORTED;
+    }
+
+    char msg[256];
+    auto cuda_fail = [&](const char *what, cudaError_t e) {
+        std::snprintf(msg, sizeof(msg), "%s: %s", what, cudaGetErrorString(e));
+        copy_msg(why, why_len, msg);
+        return GG_ERR_CUDA;
+    };
+
+    // ---- per-device set-up on the first call ----
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return cuda_fail("cudaGetDevice", e);
+    if (dev < 0 || dev >= kNoAllocMaxDevices) {
+        copy_msg(why, why_len, "device ordinal out of range");
+        return GG_ERR_ARG;
+    }
+    int cc_major = 0, cc_minor = 0;
+    if ((e = cudaDeviceGetAttribute(&cc_major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&cc_minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+        return cuda_fail("cudaDeviceGetAttribute", e);
+    if (cc_major != 10 || cc_minor != 0) {
+        copy_msg(why, why_len, "needs an sm_100 GPU (B200/GB200)");
+        return GG_NOT_SUPPORTED;
+    }
+    NoAllocDevice *d = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+        d = &g_noalloc_dev[dev];
+        if (!d->ready && (e = noalloc_device_setup(dev, *d)) != cudaSuccess)
+            return cuda_fail("gg_run_noalloc device set-up", e);
+    }
+    EncodeTiledFn encode = get_encode_fn();
+    if (!encode) {
+        copy_msg(why, why_len, "cuTensorMapEncodeTiled not available from the driver");
+        return GG_ERR_CUDA;
+    }
+
+    // ---- variant, group arguments (host stack), descriptors ----
+    const int vi = choose_variant(p, d->num_sms);
+    const Variant &v = variant_at(vi);
+    const int G = p->group_num;
+    const int64_t tiles_n = (p->n + v.bn - 1) / v.bn;
+    int32_t meta[2 * (kNoAllocMaxGroups + 1)];
+    int64_t tiles = 0, rows = 0;
+    for (int g = 0; g < G; ++g) {
+        meta[g] = int32_t(tiles);
+        meta[G + 1 + g] = int32_t(rows);
+        tiles += (p->group_m[g] + v.cluster_m - 1) / v.cluster_m * tiles_n;
+        rows += p->group_m[g];
+    }
+    if (tiles >= (int64_t(1) << 31)) {
+        copy_msg(why, why_len, "too many tiles");
+        return GG_NOT_SUPPORTED;
+    }
+    meta[G] = int32_t(tiles);
+    meta[2 * G + 1] = int32_t(rows);
+    if (tiles == 0)
+        return GG_OK;  // every group empty: nothing to write
+
+    uint32_t *d_status = reinterpret_cast<uint32_t *>(d->scratch);
+    int32_t *d_meta = reinterpret_cast<int32_t *>(d->scratch + kNoAllocHeader);
+    // The previous call's status and offsets are still in the array: clear the status word and
+    // overwrite the offsets, in stream order behind any earlier call on the same stream.
+    if ((e = cudaMemsetAsync(d_status, 0, sizeof(uint32_t), stream)) != cudaSuccess)
+        return cuda_fail("cudaMemsetAsync(status)", e);
+    if ((e = cudaMemcpyAsync(d_meta, meta, size_t(2 * (G + 1)) * sizeof(int32_t), cudaMemcpyHostToDevice,
+                             stream)) != cudaSuccess)
+        return cuda_fail("cudaMemcpyAsync(group offsets)", e);
+
+    const CUtensorMapDataType dt =
+        p->dtype == GG_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap tmap_a, tmap_b;
+    const cuuint32_t estride[3] = {1, 1, 1};
+    const cuuint64_t a_dim[2] = {cuuint64_t(p->k), cuuint64_t(total_m)};
+    const cuuint64_t a_stride[1] = {cuuint64_t(p->k) * 2};
+    const cuuint32_t a_box[2] = {gg::kBK, gg::kBM};
+    if (encode(&tmap_a, dt, 2, const_cast<void *>(p->x), a_dim, a_stride, a_box, estride,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        copy_msg(why, why_len, "cuTensorMapEncodeTiled(x) failed");
+        return GG_ERR_CUDA;
+    }
+    const cuuint64_t b_dim[3] = {cuuint64_t(p->k), cuuint64_t(p->n), cuuint64_t(G)};
+    const cuuint64_t b_stride[2] = {cuuint64_t(p->k) * 2, cuuint64_t(p->n) * cuuint64_t(p->k) * 2};
+    const cuuint32_t b_box[3] = {gg::kBK, cuuint32_t(v.bn / v.cg), 1};
+    if (encode(&tmap_b, dt, 3, const_cast<void *>(p->w), b_dim, b_stride, b_box, estride,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        copy_msg(why, why_len, "cuTensorMapEncodeTiled(w) failed");
+        return GG_ERR_CUDA;
+    }
+
+    gg::KernelParams kp{};
+    kp.tile_off = d_meta;
+    kp.row_off = d_meta + (G + 1);
+    kp.out = p->out;
+    kp.status = d_status;
+    kp.group_num = G;
+    kp.n = int32_t(p->n);
+    kp.k = int32_t(p->k);
+    kp.num_kb = int32_t((p->k + gg::kBK - 1) / gg::kBK);
+    kp.tiles_n = int32_t(tiles_n);
+    kp.total_tiles = int32_t(tiles);
+    kp.band = v.cg == 2 ? 8 : 16;
+    kp.timeout_ns = 2000ull * 1000000ull;
+
+    const int slots = v.cg == 2 ? 2 * d->clusters_v0 : d->num_sms;
+    if (slots < v.cg) {
+        copy_msg(why, why_len, "no CTA of this kernel fits on the device");
+        return GG_NOT_SUPPORTED;
+    }
+    const int grid = int(std::max<int64_t>(v.cg, std::min<int64_t>(slots, tiles * v.cg)));
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(v.cg);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(unsigned(grid), 1, 1);
+    cfg.blockDim = dim3(gg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = size_t(v.smem);
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *args[3] = {&tmap_a, &tmap_b, &kp};
+    if ((e = cudaLaunchKernelExC(&cfg, p->dtype == GG_BF16 ? v.fn_bf16 : v.fn_fp16, args)) != cudaSuccess)
+        return cuda_fail("kernel launch", e);
+
+    if (status_out) {
+        uint32_t st = 0;
+        if ((e = cudaMemcpyAsync(&st, d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream)) != cudaSuccess)
+            return cuda_fail("cudaMemcpyAsync(status)", e);
+        if ((e = cudaStreamSynchronize(stream)) != cudaSuccess)
+            return cuda_fail("cudaStreamSynchronize", e);
+        *status_out = st;
+        if (st != 0) {
+            std::snprintf(msg, sizeof(msg), "kernel bounded wait timed out: status 0x%x", st);
+            copy_msg(why, why_len, msg);
+            return GG_ERR_DEVICE;
+        }
+    }
+    return GG_OK;
+}

@@ -117,6 +117,28 @@ int gg_expert_shard(int32_t group_num, int32_t world, int32_t rank, int32_t *g0,
 /* Library ABI version (incremented on incompatible change). */
 int gg_abi_version(void);
 
+/* One grouped GEMM with no allocation at all: the same computation and result as
+ * gg_prepare() + gg_run(), for callers that cannot allocate device memory when they call, e.g. an
+ * engine that has reserved the GPU's memory for its own pool, a plugin host with a fixed memory
+ * budget, or a latency-critical path that must not call cudaMalloc/cudaFree (they can
+ * synchronise the device). No counterpart in the reference, whose backend allocates its
+ * argument buffer in prepare (ck_kernel/ck_grouped_gemm.cpp:209).
+ *
+ * The per-group tile/row offsets and the kernel's status word live in one fixed device array
+ * inside the library (about 8 KB, held by every GPU that loads the library until the process
+ * exits), so group_num is limited to 1024; larger problems are refused with GG_NOT_SUPPORTED and
+ * a reason in `why`. Nothing is allocated, neither device memory nor host heap memory.
+ * Enqueues on `stream` and returns without waiting, unless `status_out` is non-NULL: then it
+ * waits for the kernel and stores its status word there (0 = every bounded wait finished;
+ * GG_ERR_DEVICE is returned otherwise).
+ *
+ * The first call on each device does a one-time set-up (it looks up the array's device address
+ * and the kernels' launch limits); make that first call before any stream capture. Every call
+ * on a device shares the one array and each call overwrites it, so calls whose kernels may
+ * overlap on the GPU (different streams without ordering between them) race; calls in order on
+ * one stream do not. Errors are reported in `why` (there is no handle for gg_last_error). */
+int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t *status_out, char *why, size_t why_len);
+
 #ifdef __cplusplus
 }
 #endif
