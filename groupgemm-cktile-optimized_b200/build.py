@@ -29,10 +29,10 @@ TARGETS = {
         "flags": ["-Xcompiler", "-fPIC", "-shared"],
     },
     "gg_bench": {
-        "srcs": ["gg_bench_main.cu", "gg_backend.cpp", "gg_capi.cu"],
-        "deps": ["gg_bench_main.cu", "gg_backend.cpp", "gg_capi.cu", "gg_kernel.cuh", "gg_ptx.cuh",
+        "srcs": ["gg_bench_main.cu", "gg_cublas_backends.cpp", "gg_capi.cu"],
+        "deps": ["gg_bench_main.cu", "gg_cublas_backends.cpp", "gg_capi.cu", "gg_kernel.cuh", "gg_ptx.cuh",
                  os.path.join("..", "..", "include", "gg_backend.hpp")],
-        "flags": [],
+        "flags": ["-lcublas"],
     },
 }
 

@@ -88,6 +88,7 @@ struct gg_handle {
     int opt_band = 0;
     int opt_max_ctas = 0;
     int64_t opt_timeout_ms = 2000;
+    int opt_test_stall = 0;
 
     // prepared state
     bool ready = false;
@@ -195,6 +196,10 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < 1 || value > 60000)
             return fail(h, GG_ERR_ARG, "timeout_ms must be 1..60000");
         h->opt_timeout_ms = value;
+    } else if (!std::strcmp(key, "test_stall")) {
+        if (value != 0 && value != 1)
+            return fail(h, GG_ERR_ARG, "test_stall must be 0 or 1");
+        h->opt_test_stall = int(value);
     } else {
         return fail(h, GG_ERR_ARG, "unknown option '%s'", key);
     }
@@ -387,6 +392,7 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     kp.tiles_n = int32_t(tiles_n);
     kp.total_tiles = int32_t(tiles);
     kp.band = band;
+    kp.test_stall = h->opt_test_stall;
     kp.timeout_ns = uint64_t(h->opt_timeout_ms) * 1000000ull;
 
     GG_CUDA(h, cudaStreamSynchronize(stream));

@@ -68,7 +68,8 @@ struct KernelParams {
     int32_t tiles_n;      // ceil(N / BN)
     int32_t total_tiles;  // tile_off[G]
     int32_t band;         // M tiles per raster band (L2 reuse of the weight panel)
-    int32_t pad_;
+    int32_t test_stall;   // test only: 1 = the first stage of cluster 0 is never loaded, so the
+                          // MMA wait on it runs out and the status word reports it
     uint64_t timeout_ns;
 };
 
@@ -263,11 +264,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t a_dst = smem_base + uint32_t(s) * C::kStageBytes;
                     const uint32_t b_dst = a_dst + C::kABytes;
                     const uint32_t fb = full_leader0 + 8u * s;
-                    if (leader)
+                    // test hook: the leader skips its arrive and loads of cluster 0's first stage
+                    const bool skip = p.test_stall != 0 && cluster_id == 0 && leader && ks == 0 && t == cluster_id;
+                    if (leader && !skip)
                         ptx::mbar_arrive_expect_tx(full_bar(s), uint32_t(kCG * na * (C::kAAtomBytes + C::kBAtomBytes)));
 #pragma unroll
                     for (int a = 0; a < kAtoms; ++a) {
-                        if (a < na) {
+                        if (a < na && !skip) {
                             const int k0 = (ks * kAtoms + a) * kBK;
                             if constexpr (kCG == 1) {
                                 ptx::tma_load_2d(a_dst + a * C::kAAtomBytes, &tmap_a, fb, k0, a_row);

@@ -101,6 +101,9 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
  *   "band"       M tiles per raster band (default chosen per shape), 0 = auto
  *   "max_ctas"   cap on the persistent grid (0 = one CTA per SM)
  *   "timeout_ms" bounded-wait limit inside the kernel (default 2000)
+ *   "test_stall" test only: 1 = the kernel never loads the first stage of its first CTA (pair),
+ *                so that wait runs out after timeout_ms and gg_device_status() reports it;
+ *                used to test failure detection without faulting the GPU
  * Returns GG_OK or GG_ERR_ARG for an unknown key. The knobs are the analogue of the compile-time
  * CkTileConfig (ck_kernel/ck_grouped_gemm_config.hpp:26-86) that the reference edits to tune. */
 int gg_set_option(gg_handle *h, const char *key, int64_t value);

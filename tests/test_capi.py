@@ -59,7 +59,8 @@ def test_set_option(gg):
     b.set_option("band", 4)
     b.set_option("timeout_ms", 500)
     b.set_option("max_ctas", 64)
-    for key, val in (("variant", 7), ("band", -1), ("timeout_ms", 0), ("bogus", 1)):
+    b.set_option("test_stall", 0)
+    for key, val in (("variant", 7), ("band", -1), ("timeout_ms", 0), ("test_stall", 2), ("bogus", 1)):
         with pytest.raises(gg.GGError):
             b.set_option(key, val)
 
