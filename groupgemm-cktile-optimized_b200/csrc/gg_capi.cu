@@ -86,6 +86,7 @@ struct gg_handle {
     // options
     int opt_variant = -1;
     int opt_band = 0;
+    int opt_bn = 0;
     int opt_max_ctas = 0;
     int64_t opt_timeout_ms = 2000;
     int opt_test_stall = 0;
@@ -137,31 +138,65 @@ int refuse(gg_handle *h, char *why, size_t why_len, const char *msg) {
             return fail((h), GG_ERR_CUDA, "%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__); \
     } while (0)
 
-int64_t tiles_for(const gg_problem *p, const Variant &v) {
-    const int64_t tn = (p->n + v.bn - 1) / v.bn;
+int64_t tiles_for(const gg_problem *p, const Variant &v, int bn) {
+    const int64_t tn = (p->n + bn - 1) / bn;
     int64_t t = 0;
     for (int g = 0; g < p->group_num; ++g)
         t += (p->group_m[g] + v.cluster_m - 1) / v.cluster_m * tn;
     return t;
 }
 
-// Automatic variant choice (measured on B200: the 256x256 pair tile has the highest rate per SM,
-// then 128x256, then 128x128, but small problems are bound by one tile's latency):
-//   1. the whole problem fits in one wave of 128x128 tiles -> 128x128 (least work per CTA);
-//   2. at least one full wave of 256x256 pair tiles        -> 256x256;
-//   3. one wave of 128x256 tiles                           -> 128x256 (as many SMs, half the
-//                                                             work per SM of a pair tile);
-//   4. otherwise                                           -> 256x256.
-// Low-tile-count shapes are where the reference loses to hipBLASLt (README.md:56-58).
-int choose_variant(const gg_problem *p, int num_sms) {
-    if (tiles_for(p, variant_at(2)) <= num_sms)
-        return 2;
-    if (tiles_for(p, variant_at(0)) >= num_sms / 2)
-        return 0;
-    if (tiles_for(p, variant_at(1)) <= num_sms)
-        return 1;
-    return 0;
+struct Choice {
+    int variant;
+    int bn;
+};
+
+// Model of one launch in MMA-issue cycles per SM: waves x K-atoms x 4 MMAs x cycles per MMA.
+// A tcgen05.mma of 128 rows x bn x 16 per SM keeps the tensor pipe busy bn/2 cycles, but the
+// single issuing thread needs ~85 cycles per MMA plus the per-stage wait/commit share (~20 cycles
+// per MMA with two K atoms per stage, ~45 with one). Measured on B200 this reproduces the rate
+// ratios of the three variants on large problems (1 : 0.85 : 0.69). Waves count whole, so the
+// model trades tile width against wave quantisation and M/N tail waste.
+double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots_pairs_or_ctas) {
+    const int64_t tiles = tiles_for(p, v, bn);
+    const int64_t waves = (tiles + slots_pairs_or_ctas - 1) / slots_pairs_or_ctas;
+    const double per_mma = std::max(bn / 2.0, 85.0) + (v.atoms >= 2 ? 20.0 : 45.0);
+    const int64_t atoms = (p->k + gg::kBK - 1) / gg::kBK;
+    // A CTA pair pays a fixed start-up cost (cluster barrier, cross-CTA pipeline fill) that only
+    // matters for launches of a few microseconds.
+    const double fixed = v.cg == 2 ? 1500.0 : 0.0;
+    return double(waves) * double(atoms) * 4.0 * per_mma + fixed;
 }
+
+// Pick the variant and tile width with the smallest modelled time. `forced_variant` >= 0 and
+// `forced_bn` > 0 restrict the search. `pairs` is the number of co-resident CTA pairs of the
+// 2-CTA variant.
+Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_variant, int forced_bn) {
+    Choice best{-1, 0};
+    double best_t = 0;
+    for (int vi = 0; vi < 3; ++vi) {
+        if (forced_variant >= 0 && vi != forced_variant)
+            continue;
+        const Variant &v = variant_at(vi);
+        const int slots = v.cg == 2 ? pairs : num_sms;
+        if (slots < 1)
+            continue;
+        for (int bn = v.bn; bn >= 32; bn -= 32) {
+            if (forced_bn > 0 && bn != forced_bn)
+                continue;
+            if (forced_bn <= 0 && bn < 128)
+                continue;  // narrower tiles are issue-bound; only on request
+            const double t = model_cycles(p, v, bn, slots);
+            if (best.variant < 0 || t < best_t * 0.999) {
+                best = {vi, bn};
+                best_t = t;
+            }
+        }
+    }
+    return best;
+}
+
+
 
 }  // namespace
 
@@ -188,6 +223,10 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < 0 || value > 1024)
             return fail(h, GG_ERR_ARG, "band must be 0..1024");
         h->opt_band = int(value);
+    } else if (!std::strcmp(key, "bn")) {
+        if (value != 0 && (value < 32 || value > 256 || value % 32 != 0))
+            return fail(h, GG_ERR_ARG, "bn must be 0 (auto) or a multiple of 32 in 32..256");
+        h->opt_bn = int(value);
     } else if (!std::strcmp(key, "max_ctas")) {
         if (value < 0)
             return fail(h, GG_ERR_ARG, "max_ctas must be >= 0");
@@ -290,13 +329,42 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     if (!encode)
         return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
 
-    const int vi = h->opt_variant >= 0 ? h->opt_variant : choose_variant(p, num_sms);
+    // Co-resident CTA pairs of the 2-CTA variant (the cost model's slot count for it).
+    int pairs = 0;
+    {
+        const Variant &v0 = variant_at(0);
+        const void *fn0 = p->dtype == GG_BF16 ? v0.fn_bf16 : v0.fn_fp16;
+        GG_CUDA(h, cudaFuncSetAttribute(fn0, cudaFuncAttributeMaxDynamicSharedMemorySize, v0.smem));
+        cudaLaunchConfig_t cfg{};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(num_sms, 1, 1);
+        cfg.blockDim = dim3(gg::kThreads, 1, 1);
+        cfg.dynamicSmemBytes = size_t(v0.smem);
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        GG_CUDA(h, cudaOccupancyMaxActiveClusters(&pairs, fn0, &cfg));
+    }
+    if (h->opt_max_ctas > 0) {
+        pairs = std::min(pairs, h->opt_max_ctas / 2);
+        num_sms = std::min(num_sms, h->opt_max_ctas);
+    }
+    if (h->opt_bn > 0 && h->opt_variant >= 0 && h->opt_bn > variant_at(h->opt_variant).bn)
+        return refuse(h, why, why_len, "bn is wider than the variant's tile");
+    const Choice ch = choose_tiling(p, num_sms, pairs, h->opt_variant, h->opt_bn);
+    if (ch.variant < 0)
+        return refuse(h, why, why_len, "no kernel variant fits this device and these options");
+    const int vi = ch.variant;
+    const int bn = ch.bn;
     const Variant &v = variant_at(vi);
     const void *fn = p->dtype == GG_BF16 ? v.fn_bf16 : v.fn_fp16;
 
-    // ---- group arguments: tile offsets (this variant's tile) and row offsets ----
+    // ---- group arguments: tile offsets (this tiling) and row offsets ----
     const int G = p->group_num;
-    const int64_t tiles_n = (p->n + v.bn - 1) / v.bn;
+    const int64_t tiles_n = (p->n + bn - 1) / bn;
     std::vector<int32_t> meta(2 * size_t(G + 1));
     int64_t tiles = 0, rows = 0;
     for (int g = 0; g < G; ++g) {
@@ -339,7 +407,7 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
             return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed: %d", int(r));
         const cuuint64_t b_dim[3] = {cuuint64_t(p->k), cuuint64_t(p->n), cuuint64_t(G)};
         const cuuint64_t b_stride[2] = {cuuint64_t(p->k) * 2, cuuint64_t(p->n) * cuuint64_t(p->k) * 2};
-        const cuuint32_t b_box[3] = {gg::kBK, cuuint32_t(v.bn / v.cg), 1};
+        const cuuint32_t b_box[3] = {gg::kBK, cuuint32_t(bn / v.cg), 1};
         r = encode(&h->tmap_b, dt, 3, const_cast<void *>(p->w), b_dim, b_stride, b_box, estride,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -354,27 +422,7 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
         band = v.cg == 2 ? 8 : 16;
     }
     GG_CUDA(h, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem));
-    int slots = 0;  // CTAs that can be resident at once
-    if (v.cg == 2) {
-        cudaLaunchConfig_t cfg{};
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.gridDim = dim3(num_sms, 1, 1);
-        cfg.blockDim = dim3(gg::kThreads, 1, 1);
-        cfg.dynamicSmemBytes = size_t(v.smem);
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        int clusters = 0;
-        GG_CUDA(h, cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg));
-        slots = 2 * clusters;
-    } else {
-        slots = num_sms;
-    }
-    if (h->opt_max_ctas > 0)
-        slots = std::min(slots, std::max(v.cg, h->opt_max_ctas / v.cg * v.cg));
+    const int slots = v.cg == 2 ? 2 * pairs : num_sms;  // CTAs that can be resident at once
     if (slots < v.cg)
         return refuse(h, why, why_len, "no CTA of this kernel fits on the device");
     const int64_t want = tiles * v.cg;
@@ -390,6 +438,7 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     kp.k = int32_t(p->k);
     kp.num_kb = int32_t((p->k + gg::kBK - 1) / gg::kBK);
     kp.tiles_n = int32_t(tiles_n);
+    kp.bn = bn;
     kp.total_tiles = int32_t(tiles);
     kp.band = band;
     kp.test_stall = h->opt_test_stall;
@@ -406,7 +455,7 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     h->cg = v.cg;
     char d[256];
     std::snprintf(d, sizeof(d), "gg_sm100<%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld grid=%d band=%d",
-                  p->dtype == GG_BF16 ? "bf16" : "fp16", v.cluster_m, v.bn, gg::kBK * v.atoms, v.cg, v.stages,
+                  p->dtype == GG_BF16 ? "bf16" : "fp16", v.cluster_m, bn, gg::kBK * v.atoms, v.cg, v.stages,
                   (long long)tiles, h->grid, band);
     h->detail = d;
     h->ready = true;
@@ -618,10 +667,15 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
     }
 
     // ---- variant, group arguments (host stack), descriptors ----
-    const int vi = choose_variant(p, d->num_sms);
-    const Variant &v = variant_at(vi);
+    const Choice ch = choose_tiling(p, d->num_sms, d->clusters_v0, -1, 0);
+    if (ch.variant < 0) {
+        copy_msg(why, why_len, "no kernel variant fits this device");
+        return GG_NOT_SUPPORTED;
+    }
+    const Variant &v = variant_at(ch.variant);
+    const int bn = ch.bn;
     const int G = p->group_num;
-    const int64_t tiles_n = (p->n + v.bn - 1) / v.bn;
+    const int64_t tiles_n = (p->n + bn - 1) / bn;
     int32_t meta[2 * (kNoAllocMaxGroups + 1)];
     int64_t tiles = 0, rows = 0;
     for (int g = 0; g < G; ++g) {
@@ -664,7 +718,7 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
     }
     const cuuint64_t b_dim[3] = {cuuint64_t(p->k), cuuint64_t(p->n), cuuint64_t(G)};
     const cuuint64_t b_stride[2] = {cuuint64_t(p->k) * 2, cuuint64_t(p->n) * cuuint64_t(p->k) * 2};
-    const cuuint32_t b_box[3] = {gg::kBK, cuuint32_t(v.bn / v.cg), 1};
+    const cuuint32_t b_box[3] = {gg::kBK, cuuint32_t(bn / v.cg), 1};
     if (encode(&tmap_b, dt, 3, const_cast<void *>(p->w), b_dim, b_stride, b_box, estride,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
@@ -682,6 +736,7 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
     kp.k = int32_t(p->k);
     kp.num_kb = int32_t((p->k + gg::kBK - 1) / gg::kBK);
     kp.tiles_n = int32_t(tiles_n);
+    kp.bn = bn;
     kp.total_tiles = int32_t(tiles);
     kp.band = v.cg == 2 ? 8 : 16;
     kp.timeout_ns = 2000ull * 1000000ull;

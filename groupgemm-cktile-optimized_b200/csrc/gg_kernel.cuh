@@ -65,7 +65,8 @@ struct KernelParams {
     int32_t n;
     int32_t k;
     int32_t num_kb;       // ceil(K / 64): K atoms
-    int32_t tiles_n;      // ceil(N / BN)
+    int32_t tiles_n;      // ceil(N / bn)
+    int32_t bn;           // tile N of this launch: a multiple of 32, <= the variant's kBN
     int32_t total_tiles;  // tile_off[G]
     int32_t band;         // M tiles per raster band (L2 reuse of the weight panel)
     int32_t test_stall;   // test only: 1 = the first stage of cluster 0 is never loaded, so the
@@ -190,7 +191,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_sm100(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                        const __grid_constant__ KernelParams p) {
     using C = TileCfg<kCG, kBN, kAtoms>;
-    constexpr uint32_t kIdesc = ptx::f16_idesc(Fmt<T>::kUmma, kBM * kCG, kBN);
+    // Tile N is a launch parameter (multiple of 32, at most kBN): the smem ring and TMEM are sized
+    // for kBN, a narrower tile uses the first bn/kCG weight rows of each atom and bn columns of
+    // each accumulator.
+    const int bn = p.bn;
+    const int b_rows = bn / kCG;
+    const uint32_t idesc = ptx::f16_idesc(Fmt<T>::kUmma, kBM * kCG, bn);
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the 128-byte swizzle atoms.
@@ -253,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = cluster_id; t < p.total_tiles && ok; t += num_clusters) {
                 const TileCoord tc = decode_tile<C::kClusterM>(p, t, cursor);
                 const int a_row = __ldg(&p.row_off[tc.g]) + tc.mt * C::kClusterM + int(cta_rank) * kBM;
-                const int b_row = tc.nt * kBN + int(cta_rank) * C::kBRows;
+                const int b_row = tc.nt * bn + int(cta_rank) * b_rows;
                 for (int ks = 0; ks < num_ks; ++ks) {
                     if (!wait_one(empty_bar(s), ph ^ 1u, ab, kStatusTimeout | kRoleProducer | uint32_t(s))) {
                         ok = false;
@@ -267,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // test hook: the leader skips its arrive and loads of cluster 0's first stage
                     const bool skip = p.test_stall != 0 && cluster_id == 0 && leader && ks == 0 && t == cluster_id;
                     if (leader && !skip)
-                        ptx::mbar_arrive_expect_tx(full_bar(s), uint32_t(kCG * na * (C::kAAtomBytes + C::kBAtomBytes)));
+                        ptx::mbar_arrive_expect_tx(full_bar(s), uint32_t(kCG * na * (C::kAAtomBytes + b_rows * kBK * 2)));
 #pragma unroll
                     for (int a = 0; a < kAtoms; ++a) {
                         if (a < na && !skip) {
@@ -333,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 // atom a, then 16 elements (32 bytes) along K inside the swizzle atom
                                 const uint64_t da = uint64_t((a * C::kAAtomBytes + kk * 32) >> 4);
                                 const uint64_t db = uint64_t((a * C::kBAtomBytes + kk * 32) >> 4);
-                                ptx::umma_f16<kCG>(d_tmem, adesc + da, bdesc + db, kIdesc,
+                                ptx::umma_f16<kCG>(d_tmem, adesc + da, bdesc + db, idesc,
                                                    (ks | a | kk) != 0 ? 1u : 0u);
                             }
                         }
@@ -380,11 +386,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             T *orow = out + (int64_t(g_row0) + local_row) * p.n;
             const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * kBN);
 #pragma unroll 1
-            for (int c = 0; c < kBN / 32; ++c) {
+            for (int c = 0; c < bn / 32; ++c) {
                 uint32_t r[32];
                 ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
                 ptx::tmem_wait_ld(r);
-                const int col = tc.nt * kBN + c * 32;
+                const int col = tc.nt * bn + c * 32;
                 if (row_ok) {
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {

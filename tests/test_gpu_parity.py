@@ -33,7 +33,7 @@ def upload(torch, bits):
     return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).cuda()
 
 
-def run_backend(gg, group_m, n, k, dtype, xd, wd, variant=-1, band=0, stream=None):
+def run_backend(gg, group_m, n, k, dtype, xd, wd, variant=-1, band=0, stream=None, bn=0):
     """Run one prepared grouped GEMM; returns (out bits [sum(M), n], detail)."""
     torch = _torch()
     total = int(sum(group_m))
@@ -43,6 +43,8 @@ def run_backend(gg, group_m, n, k, dtype, xd, wd, variant=-1, band=0, stream=Non
         b.set_option("variant", variant)
     if band:
         b.set_option("band", band)
+    if bn:
+        b.set_option("bn", bn)
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     why = b.prepare(dtype, group_m, n, k, xd.data_ptr() if xd.numel() else 0, wd.data_ptr(),
                     out.data_ptr(), s)
@@ -94,6 +96,20 @@ def test_unbalanced_and_empty_groups(gg, orc, dtype):
     # Real MoE routing: zero-length groups, groups smaller than a tile, tiles straddling groups.
     group_m = [0, 1, 127, 128, 129, 0, 300, 5, 0, 257]
     full_case(gg, orc, group_m, 264, 200, dtype, ALL_VARIANTS)
+
+
+@pytest.mark.parametrize("variant,bn", [(0, 224), (0, 192), (0, 160), (0, 128), (0, 64), (1, 192),
+                                        (1, 96), (1, 32), (2, 96)])
+def test_narrow_tile_widths(gg, orc, variant, bn):
+    # tile N is a launch parameter; N is not a multiple of any of these widths
+    torch = _torch()
+    group_m, n, k = [300, 0, 17, 513], 1000, 320
+    x, w = orc.make_inputs(group_m, n, k, 1)
+    xd, wd = upload(torch, x), upload(torch, w)
+    got, detail = run_backend(gg, group_m, n, k, 1, xd, wd, variant=variant, bn=bn)
+    assert f"x{bn}x" in detail, detail
+    bad, mx, first = orc.check16(got, orc.grouped_gemm_f32(x, w, group_m, 1), 1)
+    assert bad == 0, (detail, bad, mx, first)
 
 
 def test_all_groups_empty_is_a_no_op(gg, orc):
