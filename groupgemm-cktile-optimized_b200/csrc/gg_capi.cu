@@ -87,6 +87,7 @@ struct gg_handle {
     int opt_variant = -1;
     int opt_band = 0;
     int opt_bn = 0;
+    int opt_split = 0;
     int opt_max_ctas = 0;
     int64_t opt_timeout_ms = 2000;
     int opt_test_stall = 0;
@@ -100,6 +101,10 @@ struct gg_handle {
     int32_t *d_meta = nullptr;  // tile_off[G+1] then row_off[G+1]
     size_t meta_cap = 0;        // int32 entries
     uint32_t *d_status = nullptr;
+    float *d_ws = nullptr;  // split-K partial sums
+    size_t ws_cap = 0;      // bytes
+    int32_t *d_counters = nullptr;
+    size_t counters_cap = 0;  // bytes
     CUtensorMap tmap_a{}, tmap_b{};
     gg::KernelParams params{};
     int grid = 0;
@@ -149,31 +154,43 @@ int64_t tiles_for(const gg_problem *p, const Variant &v, int bn) {
 struct Choice {
     int variant;
     int bn;
+    int splits;
 };
 
-// Model of one launch in MMA-issue cycles per SM: waves x K-atoms x 4 MMAs x cycles per MMA.
-// A tcgen05.mma of 128 rows x bn x 16 per SM keeps the tensor pipe busy bn/2 cycles, but the
-// single issuing thread needs ~85 cycles per MMA plus the per-stage wait/commit share (~20 cycles
-// per MMA with two K atoms per stage, ~45 with one). Measured on B200 this reproduces the rate
-// ratios of the three variants on large problems (1 : 0.85 : 0.69). Waves count whole, so the
-// model trades tile width against wave quantisation and M/N tail waste.
-double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots_pairs_or_ctas) {
+// Model of one launch in cycles per SM: waves x K-atoms x 4 MMAs x cycles per MMA, where one
+// MMA covers 128 rows x bn x 16 per SM. The cycles per MMA are fitted to B200 measurements on a
+// large problem (config L) for each variant and width: the tensor pipe needs bn/2 cycles, but
+// the single issuing thread, the per-stage wait/commit and the L2->SM traffic (which grows as
+// tiles narrow) add a part that shrinks slower than bn. Waves count whole, so the model trades
+// tile width against wave quantisation and M/N tail waste.
+double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots_pairs_or_ctas, int splits) {
     const int64_t tiles = tiles_for(p, v, bn);
-    const int64_t waves = (tiles + slots_pairs_or_ctas - 1) / slots_pairs_or_ctas;
-    const double per_mma = std::max(bn / 2.0, 85.0) + (v.atoms >= 2 ? 20.0 : 45.0);
+    const int64_t waves = (tiles * splits + slots_pairs_or_ctas - 1) / slots_pairs_or_ctas;
+    const double per_mma = v.cg == 2 ? 0.344 * bn + 60.0 : v.atoms >= 2 ? 0.344 * bn + 63.0 : 0.396 * bn + 70.0;
     const int64_t atoms = (p->k + gg::kBK - 1) / gg::kBK;
+    const int64_t atoms_per_unit = (atoms + splits - 1) / splits;
     // A CTA pair pays a fixed start-up cost (cluster barrier, cross-CTA pipeline fill) that only
     // matters for launches of a few microseconds.
-    const double fixed = v.cg == 2 ? 1500.0 : 0.0;
-    return double(waves) * double(atoms) * 4.0 * per_mma + fixed;
+    double fixed = v.cg == 2 ? 1500.0 : 0.0;
+    if (splits > 1) {
+        // split-K: fp32 partials written by every split and read back by the last one
+        int64_t total_m = 0;
+        for (int g = 0; g < p->group_num; ++g)
+            total_m += p->group_m[g];
+        const double bytes = 2.0 * double(splits) * double(total_m) * double(p->n) * 4.0;
+        fixed += 3000.0 + bytes / 2000.0;  // ~2 KB per SM-clock of L2/HBM bandwidth, whole GPU
+    }
+    return double(waves) * double(atoms_per_unit) * 4.0 * per_mma + fixed;
 }
 
 // Pick the variant and tile width with the smallest modelled time. `forced_variant` >= 0 and
 // `forced_bn` > 0 restrict the search. `pairs` is the number of co-resident CTA pairs of the
 // 2-CTA variant.
-Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_variant, int forced_bn) {
-    Choice best{-1, 0};
+Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_variant, int forced_bn,
+                     int max_splits = 1) {
+    Choice best{-1, 0, 1};
     double best_t = 0;
+    const int64_t atoms = (p->k + gg::kBK - 1) / gg::kBK;
     for (int vi = 0; vi < 3; ++vi) {
         if (forced_variant >= 0 && vi != forced_variant)
             continue;
@@ -186,10 +203,16 @@ Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_var
                 continue;
             if (forced_bn <= 0 && bn < 128)
                 continue;  // narrower tiles are issue-bound; only on request
-            const double t = model_cycles(p, v, bn, slots);
-            if (best.variant < 0 || t < best_t * 0.999) {
-                best = {vi, bn};
-                best_t = t;
+            const int64_t tiles = tiles_for(p, v, bn);
+            for (int s = 1; s <= max_splits; ++s) {
+                // split only below one full wave, and only with >= 8 K atoms per split
+                if (s > 1 && (tiles >= slots || atoms < 8 * s || tiles * s > 4 * int64_t(slots)))
+                    break;
+                const double t = model_cycles(p, v, bn, slots, s);
+                if (best.variant < 0 || t < best_t * 0.999) {
+                    best = {vi, bn, s};
+                    best_t = t;
+                }
             }
         }
     }
@@ -223,6 +246,10 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < 0 || value > 1024)
             return fail(h, GG_ERR_ARG, "band must be 0..1024");
         h->opt_band = int(value);
+    } else if (!std::strcmp(key, "split")) {
+        if (value < 0 || value > 8)
+            return fail(h, GG_ERR_ARG, "split must be 0 (auto) or 1..8");
+        h->opt_split = int(value);
     } else if (!std::strcmp(key, "bn")) {
         if (value != 0 && (value < 32 || value > 256 || value % 32 != 0))
             return fail(h, GG_ERR_ARG, "bn must be 0 (auto) or a multiple of 32 in 32..256");
@@ -252,8 +279,16 @@ void gg_release(gg_handle *h) {
         cudaFree(h->d_meta);
     if (h->d_status)
         cudaFree(h->d_status);
+    if (h->d_ws)
+        cudaFree(h->d_ws);
+    if (h->d_counters)
+        cudaFree(h->d_counters);
     h->d_meta = nullptr;
     h->d_status = nullptr;
+    h->d_ws = nullptr;
+    h->d_counters = nullptr;
+    h->ws_cap = 0;
+    h->counters_cap = 0;
     h->meta_cap = 0;
     h->ready = false;
     h->detail.clear();
@@ -354,7 +389,18 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     }
     if (h->opt_bn > 0 && h->opt_variant >= 0 && h->opt_bn > variant_at(h->opt_variant).bn)
         return refuse(h, why, why_len, "bn is wider than the variant's tile");
-    const Choice ch = choose_tiling(p, num_sms, pairs, h->opt_variant, h->opt_bn);
+    // split-K candidates: auto (up to 4) unless forced; never when the fp32 partials would be large
+    int max_splits = h->opt_split > 0 ? h->opt_split : 4;
+    if (double(total_m) * double(p->n) * 4.0 * max_splits > 512.0 * (1 << 20))
+        max_splits = h->opt_split > 0 ? h->opt_split : 1;
+    Choice ch = choose_tiling(p, num_sms, pairs, h->opt_variant, h->opt_bn, max_splits);
+    if (h->opt_split > 0 && ch.variant >= 0) {
+        // forced split count: keep the chosen tiling, use exactly that many splits
+        const int64_t atoms = (p->k + gg::kBK - 1) / gg::kBK;
+        if (h->opt_split > atoms)
+            return refuse(h, why, why_len, "split exceeds the number of 64-wide K atoms");
+        ch.splits = h->opt_split;
+    }
     if (ch.variant < 0)
         return refuse(h, why, why_len, "no kernel variant fits this device and these options");
     const int vi = ch.variant;
@@ -389,6 +435,27 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     if (!h->d_status)
         GG_CUDA(h, cudaMalloc(&h->d_status, 16));
     GG_CUDA(h, cudaMemsetAsync(h->d_status, 0, 16, stream));
+    if (ch.splits > 1) {
+        const size_t ws_bytes = size_t(ch.splits) * size_t(total_m) * size_t(p->n) * sizeof(float);
+        const size_t ctr_bytes = size_t(tiles) * size_t(v.cg) * 4 * sizeof(int32_t);
+        if (h->ws_cap < ws_bytes) {
+            if (h->d_ws)
+                cudaFree(h->d_ws);
+            h->d_ws = nullptr;
+            h->ws_cap = 0;
+            GG_CUDA(h, cudaMalloc(&h->d_ws, ws_bytes));
+            h->ws_cap = ws_bytes;
+        }
+        if (h->counters_cap < ctr_bytes) {
+            if (h->d_counters)
+                cudaFree(h->d_counters);
+            h->d_counters = nullptr;
+            h->counters_cap = 0;
+            GG_CUDA(h, cudaMalloc(&h->d_counters, ctr_bytes));
+            h->counters_cap = ctr_bytes;
+        }
+        GG_CUDA(h, cudaMemsetAsync(h->d_counters, 0, ctr_bytes, stream));
+    }
     GG_CUDA(h, cudaMemcpyAsync(h->d_meta, meta.data(), meta.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
                                stream));
 
@@ -425,7 +492,7 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     const int slots = v.cg == 2 ? 2 * pairs : num_sms;  // CTAs that can be resident at once
     if (slots < v.cg)
         return refuse(h, why, why_len, "no CTA of this kernel fits on the device");
-    const int64_t want = tiles * v.cg;
+    const int64_t want = tiles * ch.splits * v.cg;
     h->grid = int(std::max<int64_t>(v.cg, std::min<int64_t>(slots, want)));
 
     gg::KernelParams &kp = h->params;
@@ -440,6 +507,10 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     kp.tiles_n = int32_t(tiles_n);
     kp.bn = bn;
     kp.total_tiles = int32_t(tiles);
+    kp.splits = ch.splits;
+    kp.ws = ch.splits > 1 ? h->d_ws : nullptr;
+    kp.counters = ch.splits > 1 ? h->d_counters : nullptr;
+    kp.ws_stride = total_m * p->n;
     kp.band = band;
     kp.test_stall = h->opt_test_stall;
     kp.timeout_ns = uint64_t(h->opt_timeout_ms) * 1000000ull;
@@ -454,9 +525,10 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     h->smem = v.smem;
     h->cg = v.cg;
     char d[256];
-    std::snprintf(d, sizeof(d), "gg_sm100<%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld grid=%d band=%d",
+    std::snprintf(d, sizeof(d),
+                  "gg_sm100<%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld split=%d grid=%d band=%d",
                   p->dtype == GG_BF16 ? "bf16" : "fp16", v.cluster_m, bn, gg::kBK * v.atoms, v.cg, v.stages,
-                  (long long)tiles, h->grid, band);
+                  (long long)tiles, ch.splits, h->grid, band);
     h->detail = d;
     h->ready = true;
     return GG_OK;
@@ -495,8 +567,12 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status) {
     GG_CUDA(h, cudaStreamSynchronize(stream));
     GG_CUDA(h, cudaMemcpy(status, h->d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost));
     GG_CUDA(h, cudaMemset(h->d_status, 0, sizeof(uint32_t)));
-    if (*status != 0)
+    if (*status != 0) {
+        // an aborted launch can leave split-K arrival counts behind: clear them
+        if (h->d_counters)
+            GG_CUDA(h, cudaMemset(h->d_counters, 0, h->counters_cap));
         return fail(h, GG_ERR_DEVICE, "kernel bounded wait timed out: status 0x%x", *status);
+    }
     return GG_OK;
 }
 
@@ -667,7 +743,7 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
     }
 
     // ---- variant, group arguments (host stack), descriptors ----
-    const Choice ch = choose_tiling(p, d->num_sms, d->clusters_v0, -1, 0);
+    const Choice ch = choose_tiling(p, d->num_sms, d->clusters_v0, -1, 0, 1);
     if (ch.variant < 0) {
         copy_msg(why, why_len, "no kernel variant fits this device");
         return GG_NOT_SUPPORTED;

@@ -68,6 +68,10 @@ struct KernelParams {
     int32_t tiles_n;      // ceil(N / bn)
     int32_t bn;           // tile N of this launch: a multiple of 32, <= the variant's kBN
     int32_t total_tiles;  // tile_off[G]
+    int32_t splits;       // K splits per tile (0 or 1 = none); work units = total_tiles x splits
+    float *ws;            // splits > 1: fp32 partial sums, [splits][sum(M)][N]
+    int32_t *counters;    // splits > 1: [total_tiles][kCG][4] arrival counts, 0 between launches
+    int64_t ws_stride;    // sum(M) * N
     int32_t band;         // M tiles per raster band (L2 reuse of the weight panel)
     int32_t test_stall;   // test only: 1 = the first stage of cluster 0 is never loaded, so the
                           // MMA wait on it runs out and the status word reports it
@@ -246,7 +250,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_ptr_slot;
 
     const Abort ab{p.status, abort_flag, p.timeout_ns};
-    const int num_ks = (p.num_kb + kAtoms - 1) / kAtoms;  // stages per tile
+    // Work units: every tile, or with split-K every (tile, K split). A split covers a contiguous
+    // range of K atoms; each unit runs the same producer/MMA/epilogue pipeline over its range.
+    const int splits = p.splits > 1 ? p.splits : 1;
+    const int total_units = p.total_tiles * splits;
+    const int atoms_per_split = (p.num_kb + splits - 1) / splits;
 
     if (warp == 0) {
         // ---------------- TMA producer (one thread) ----------------
@@ -256,7 +264,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            for (int t = cluster_id; t < p.total_tiles && ok; t += num_clusters) {
+            for (int u = cluster_id; u < total_units && ok; u += num_clusters) {
+                const int t = u / splits;
+                const int atom0 = (u - t * splits) * atoms_per_split;
+                const int atom1 = min(p.num_kb, atom0 + atoms_per_split);
+                const int num_ks = (atom1 - atom0 + kAtoms - 1) / kAtoms;
                 const TileCoord tc = decode_tile<C::kClusterM>(p, t, cursor);
                 const int a_row = __ldg(&p.row_off[tc.g]) + tc.mt * C::kClusterM + int(cta_rank) * kBM;
                 const int b_row = tc.nt * bn + int(cta_rank) * b_rows;
@@ -265,19 +277,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
-                    // K atoms of this stage that lie inside K (the rest would be all zero fill)
-                    const int na = min(kAtoms, p.num_kb - ks * kAtoms);
+                    // K atoms of this stage that lie inside the unit's range (the rest would be zero fill)
+                    const int na = min(kAtoms, atom1 - (atom0 + ks * kAtoms));
                     const uint32_t a_dst = smem_base + uint32_t(s) * C::kStageBytes;
                     const uint32_t b_dst = a_dst + C::kABytes;
                     const uint32_t fb = full_leader0 + 8u * s;
                     // test hook: the leader skips its arrive and loads of cluster 0's first stage
-                    const bool skip = p.test_stall != 0 && cluster_id == 0 && leader && ks == 0 && t == cluster_id;
+                    const bool skip = p.test_stall != 0 && cluster_id == 0 && leader && ks == 0 && u == cluster_id;
                     if (leader && !skip)
                         ptx::mbar_arrive_expect_tx(full_bar(s), uint32_t(kCG * na * (C::kAAtomBytes + b_rows * kBK * 2)));
 #pragma unroll
                     for (int a = 0; a < kAtoms; ++a) {
                         if (a < na && !skip) {
-                            const int k0 = (ks * kAtoms + a) * kBK;
+                            const int k0 = (atom0 + ks * kAtoms + a) * kBK;
                             if constexpr (kCG == 1) {
                                 ptx::tma_load_2d(a_dst + a * C::kAAtomBytes, &tmap_a, fb, k0, a_row);
                                 ptx::tma_load_3d(b_dst + a * C::kBAtomBytes, &tmap_b, fb, k0, b_row, tc.g);
@@ -306,16 +318,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (one thread of the pair leader) ----------------
         if (leader && lane == 0) {
-            int cursor = 0;
             uint32_t tl = 0;
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            for (int t = cluster_id; t < p.total_tiles && ok; t += num_clusters, ++tl) {
-                (void)decode_tile<C::kClusterM>(p, t, cursor);
+            for (int u = cluster_id; u < total_units && ok; u += num_clusters, ++tl) {
+                const int atom0 = (u - (u / splits) * splits) * atoms_per_split;
+                const int atom1 = min(p.num_kb, atom0 + atoms_per_split);
+                const int num_ks = (atom1 - atom0 + kAtoms - 1) / kAtoms;
                 const int acc = int(tl & 1u);
                 const uint32_t acc_ph = (tl >> 1) & 1u;
-                if (!wait_one<true>(tempty_bar(acc), acc_ph ^ 1u, ab, kStatusTimeout | kRoleMma | 0x40u | uint32_t(acc))) {
+                // The epilogue warps (also the peer's) arrive after tcgen05.wait::ld, so their reads of
+                // this accumulator are complete; a CTA-scope wait is enough before overwriting it.
+                if (!wait_one(tempty_bar(acc), acc_ph ^ 1u, ab, kStatusTimeout | kRoleMma | 0x40u | uint32_t(acc))) {
                     ok = false;
                     break;
                 }
@@ -327,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     ptx::tc_fence_after();
-                    const int na = min(kAtoms, p.num_kb - ks * kAtoms);
+                    const int na = min(kAtoms, atom1 - (atom0 + ks * kAtoms));
                     const uint32_t a_addr = smem_base + uint32_t(s) * C::kStageBytes;
                     const uint64_t adesc = ptx::sw128_kmajor_desc(a_addr);
                     const uint64_t bdesc = ptx::sw128_kmajor_desc(a_addr + C::kABytes);
@@ -360,8 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // Tail: both accumulators released by every epilogue warp of the pair.
             for (uint32_t i = tl; ok && i < tl + 2; ++i)
-                ok = wait_one<true>(tempty_bar(int(i & 1u)), ((i >> 1) & 1u) ^ 1u, ab,
-                                    kStatusTimeout | kRoleMma | 0x80u);
+                ok = wait_one(tempty_bar(int(i & 1u)), ((i >> 1) & 1u) ^ 1u, ab, kStatusTimeout | kRoleMma | 0x80u);
         }
         __syncwarp();
     } else {
@@ -372,7 +386,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         T *out = static_cast<T *>(p.out);
         int cursor = 0;
         uint32_t tl = 0;
-        for (int t = cluster_id; t < p.total_tiles; t += num_clusters, ++tl) {
+        for (int u = cluster_id; u < total_units; u += num_clusters, ++tl) {
+            const int t = u / splits;
+            const int split = u - t * splits;
             const TileCoord tc = decode_tile<C::kClusterM>(p, t, cursor);
             const int acc = int(tl & 1u);
             const uint32_t acc_ph = (tl >> 1) & 1u;
@@ -383,14 +399,78 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int m = __ldg(&p.row_off[tc.g + 1]) - g_row0;
             const int local_row = tc.mt * C::kClusterM + int(cta_rank) * kBM + row_in_cta;
             const bool row_ok = local_row < m;
-            T *orow = out + (int64_t(g_row0) + local_row) * p.n;
+            const int64_t grow = int64_t(g_row0) + local_row;
+            T *orow = out + grow * p.n;
             const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * kBN);
+            bool store_out = true;
+            if (splits > 1) {
+                // Split-K: publish this unit's fp32 partial; the last of the tile's splits to
+                // arrive (per CTA and warp) sums all of them in split order and stores out.
+                float *wrow = p.ws + int64_t(split) * p.ws_stride + grow * p.n;
 #pragma unroll 1
-            for (int c = 0; c < bn / 32; ++c) {
+                for (int c = 0; c < bn / 32; ++c) {
+                    uint32_t r[32];
+                    ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
+                    ptx::tmem_wait_ld(r);
+                    const int col = tc.nt * bn + c * 32;
+                    if (row_ok) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            if (col + j * 4 < p.n)
+                                __stcg(reinterpret_cast<float4 *>(wrow + col + j * 4),
+                                       make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+                    }
+                }
+                __threadfence();
+                __syncwarp();
+                int32_t *ctr = p.counters + (int64_t(t) * kCG + int(cta_rank)) * 4 + q;
+                int prev = 0;
+                if (lane == 0)
+                    prev = atomicAdd(ctr, 1);
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                store_out = prev == splits - 1;
+                if (store_out) {
+                    __threadfence();
+                    if (lane == 0)
+                        *ctr = 0;  // ready for the next launch
+                }
+            }
+#pragma unroll 1
+            for (int c = 0; store_out && c < bn / 32; ++c) {
                 uint32_t r[32];
                 ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
                 ptx::tmem_wait_ld(r);
                 const int col = tc.nt * bn + c * 32;
+                if (row_ok && splits > 1) {
+                    // r = sum over splits 0..splits-1 in order; this unit's own part from TMEM
+                    float sum[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        sum[j] = 0.f;
+                    for (int s2 = 0; s2 < splits; ++s2) {
+                        if (s2 == split) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                sum[j] += __uint_as_float(r[j]);
+                        } else {
+                            const float *prow = p.ws + int64_t(s2) * p.ws_stride + grow * p.n + col;
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                if (col + j * 4 < p.n) {
+                                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(prow + j * 4));
+                                    sum[4 * j] += v.x;
+                                    sum[4 * j + 1] += v.y;
+                                    sum[4 * j + 2] += v.z;
+                                    sum[4 * j + 3] += v.w;
+                                }
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        r[j] = __float_as_uint(sum[j]);
+                }
                 if (row_ok) {
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {

@@ -99,6 +99,8 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
 /* Override the automatic choices of gg_prepare (takes effect at the next gg_prepare):
  *   "variant"    -1 auto, 0 = 2-CTA 256x256 tile, 1 = 1-CTA 128x256, 2 = 1-CTA 128x128
  *   "band"       M tiles per raster band (default chosen per shape), 0 = auto
+ *   "bn"         tile width (multiple of 32, <= the variant's), 0 = auto (cost model)
+ *   "split"      K splits per tile (split-K with an fp32 workspace), 0 = auto, 1 = none
  *   "max_ctas"   cap on the persistent grid (0 = one CTA per SM)
  *   "timeout_ms" bounded-wait limit inside the kernel (default 2000)
  *   "test_stall" test only: 1 = the kernel never loads the first stage of its first CTA (pair),

@@ -62,7 +62,9 @@ def test_set_option(gg):
     b.set_option("test_stall", 0)
     b.set_option("bn", 192)
     b.set_option("bn", 0)
-    for key, val in (("variant", 7), ("band", -1), ("timeout_ms", 0), ("test_stall", 2), ("bn", 100), ("bn", 288),
+    b.set_option("split", 2)
+    b.set_option("split", 0)
+    for key, val in (("variant", 7), ("band", -1), ("timeout_ms", 0), ("test_stall", 2), ("bn", 100), ("bn", 288), ("split", 9),
                      ("bogus", 1)):
         with pytest.raises(gg.GGError):
             b.set_option(key, val)

@@ -59,3 +59,29 @@ def test_stalled_wait_reports_status_and_context_survives(gg, orc, variant):
     assert ok.device_status(s) == 0
     got = out.cpu().numpy().view(np.uint16)
     assert orc.check16(got, orc.grouped_gemm_f32(x, w, group_m, gg.BF16), gg.BF16)[0] == 0
+
+
+def test_aborted_split_k_launch_is_cleaned_up(gg, orc):
+    """A split-K launch that times out leaves arrival counters behind; gg_device_status clears
+    them, so the next launch of the same prepared problem is correct."""
+    torch = _torch()
+    group_m, n, k = [512], 1024, 2048
+    x, w = orc.make_inputs(group_m, n, k, gg.BF16)
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    wd = torch.from_numpy(w.view(np.int16)).cuda()
+    out = torch.zeros(sum(group_m) * n, dtype=torch.int16, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    b = gg.B200Backend()
+    b.set_option("variant", 0)
+    b.set_option("split", 2)
+    b.set_option("timeout_ms", 200)
+    b.set_option("test_stall", 1)
+    assert b.prepare(gg.BF16, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s) == ""
+    b.run(s)
+    assert b.device_status(s) & 0x1000
+    b.set_option("test_stall", 0)
+    assert b.prepare(gg.BF16, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s) == ""
+    b.run(s)
+    assert b.device_status(s) == 0
+    got = out.cpu().numpy().view(np.uint16)
+    assert orc.check16(got, orc.grouped_gemm_f32(x, w, group_m, gg.BF16), gg.BF16)[0] == 0

@@ -112,6 +112,37 @@ def test_narrow_tile_widths(gg, orc, variant, bn):
     assert bad == 0, (detail, bad, mx, first)
 
 
+@pytest.mark.parametrize("variant,split", [(0, 2), (0, 3), (1, 2), (1, 4), (2, 3), (0, 8)])
+def test_split_k_forced(gg, orc, variant, split):
+    """Split-K: K ranges per unit, fp32 partials, last-arriver reduction. Two launches in a row
+    (the arrival counters must be back at zero after each)."""
+    torch = _torch()
+    group_m, n, k = [300, 0, 17, 513], 1000, 1000  # K = 15.6 atoms: ragged last split
+    x, w = orc.make_inputs(group_m, n, k, 0)
+    ref = orc.grouped_gemm_f32(x, w, group_m, 0)
+    xd, wd = upload(torch, x), upload(torch, w)
+    out = torch.full((sum(group_m) * n + GUARD,), CANARY, dtype=torch.int16, device="cuda")
+    b = gg.B200Backend()
+    b.set_option("variant", variant)
+    b.set_option("split", split)
+    s = torch.cuda.current_stream().cuda_stream
+    assert b.prepare(0, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s) == ""
+    assert f"split={split}" in b.detail(), b.detail()
+    for _ in range(2):
+        out[: sum(group_m) * n].fill_(0)
+        b.run(s)
+        assert b.device_status(s) == 0
+        res = out.cpu().numpy().view(np.uint16)
+        assert np.all(res[sum(group_m) * n:] == CANARY)
+        bad, mx, first = orc.check16(res[: sum(group_m) * n].reshape(-1, n), ref, 0)
+        assert bad == 0, (b.detail(), bad, mx, first)
+
+
+def test_split_k_auto_on_low_tile_count(gg, orc):
+    # one expert, M=512, N=4096, K=14336: 32 pair tiles for 74 pairs -> the model splits K
+    full_case(gg, orc, [512], 4096, 14336, 0)
+
+
 def test_all_groups_empty_is_a_no_op(gg, orc):
     torch = _torch()
     xd = torch.empty(0, dtype=torch.int16, device="cuda")
