@@ -472,15 +472,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                         r[j] = __float_as_uint(sum[j]);
                 }
                 if (row_ok) {
+                    uint32_t h[16];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        if (col + j * 8 < p.n) {
-                            uint4 v;
-                            v.x = pack2<T>(r[8 * j + 0], r[8 * j + 1]);
-                            v.y = pack2<T>(r[8 * j + 2], r[8 * j + 3]);
-                            v.z = pack2<T>(r[8 * j + 4], r[8 * j + 5]);
-                            v.w = pack2<T>(r[8 * j + 6], r[8 * j + 7]);
-                            __stcs(reinterpret_cast<uint4 *>(orow + col + j * 8), v);
+                    for (int j = 0; j < 16; ++j)
+                        h[j] = pack2<T>(r[2 * j], r[2 * j + 1]);
+                    // whole 32-byte sectors where the row allows (N % 16 == 0 keeps rows 32-byte
+                    // aligned), else 16-byte pieces; columns past N are skipped in 8s
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        T *dst = orow + col + hh * 16;
+                        if (col + hh * 16 + 16 <= p.n && (reinterpret_cast<uintptr_t>(dst) & 31u) == 0) {
+                            ptx::st_cs_v8(dst, h[8 * hh], h[8 * hh + 1], h[8 * hh + 2], h[8 * hh + 3], h[8 * hh + 4],
+                                          h[8 * hh + 5], h[8 * hh + 6], h[8 * hh + 7]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 2; ++j)
+                                if (col + hh * 16 + j * 8 < p.n)
+                                    __stcs(reinterpret_cast<uint4 *>(dst + j * 8),
+                                           make_uint4(h[8 * hh + 4 * j], h[8 * hh + 4 * j + 1], h[8 * hh + 4 * j + 2],
+                                                      h[8 * hh + 4 * j + 3]));
                         }
                     }
                 }

@@ -134,6 +134,15 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void *tmap,
                  : "memory");
 }
 
+// 32-byte streaming store (evict-first): the 16 bf16/fp16 values of one half-chunk of a row.
+// `p` must be 32-byte aligned.
+__device__ __forceinline__ void st_cs_v8(void *p, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t a4, uint32_t a5, uint32_t a6, uint32_t a7) {
+    asm volatile("st.global.cs.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(a0), "r"(a1), "r"(a2),
+                 "r"(a3), "r"(a4), "r"(a5), "r"(a6), "r"(a7)
+                 : "memory");
+}
+
 // ---- Tensor Memory ----
 template <int kCG> __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
     if constexpr (kCG == 1)
