@@ -105,7 +105,7 @@ struct gg_handle {
     size_t ws_cap = 0;      // bytes
     int32_t *d_counters = nullptr;
     size_t counters_cap = 0;  // bytes
-    CUtensorMap tmap_a{}, tmap_b{};
+    CUtensorMap tmap_a{}, tmap_b{}, tmap_out{};
     gg::KernelParams params{};
     int grid = 0;
     const void *fn = nullptr;
@@ -480,6 +480,14 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS)
             return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(w) failed: %d", int(r));
+        // out [sum(M), N]: the epilogue's TMA stores, 32 rows x 64 columns per box
+        const cuuint64_t o_dim[2] = {cuuint64_t(p->n), cuuint64_t(total_m)};
+        const cuuint64_t o_stride[1] = {cuuint64_t(p->n) * 2};
+        const cuuint32_t o_box[2] = {64, 32};
+        r = encode(&h->tmap_out, dt, 2, p->out, o_dim, o_stride, o_box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS)
+            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(out) failed: %d", int(r));
     }
 
     // ---- raster band and persistent grid ----
@@ -553,7 +561,7 @@ int gg_run(gg_handle *h, gg_stream_t stream) {
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    void *args[3] = {&h->tmap_a, &h->tmap_b, &h->params};
+    void *args[4] = {&h->tmap_a, &h->tmap_b, &h->tmap_out, &h->params};
     GG_CUDA(h, cudaLaunchKernelExC(&cfg, h->fn, args));
     return GG_OK;
 }
@@ -801,6 +809,16 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
         copy_msg(why, why_len, "cuTensorMapEncodeTiled(w) failed");
         return GG_ERR_CUDA;
     }
+    CUtensorMap tmap_out;
+    const cuuint64_t o_dim[2] = {cuuint64_t(p->n), cuuint64_t(total_m)};
+    const cuuint64_t o_stride[1] = {cuuint64_t(p->n) * 2};
+    const cuuint32_t o_box[2] = {64, 32};
+    if (encode(&tmap_out, dt, 2, p->out, o_dim, o_stride, o_box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        copy_msg(why, why_len, "cuTensorMapEncodeTiled(out) failed");
+        return GG_ERR_CUDA;
+    }
 
     gg::KernelParams kp{};
     kp.tile_off = d_meta;
@@ -835,7 +853,7 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    void *args[3] = {&tmap_a, &tmap_b, &kp};
+    void *args[4] = {&tmap_a, &tmap_b, &tmap_out, &kp};
     if ((e = cudaLaunchKernelExC(&cfg, p->dtype == GG_BF16 ? v.fn_bf16 : v.fn_fp16, args)) != cudaSuccess)
         return cuda_fail("kernel launch", e);
 

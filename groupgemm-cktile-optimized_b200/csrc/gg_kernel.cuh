@@ -40,6 +40,10 @@
 
 #include "gg_ptx.cuh"
 
+#ifndef GG_TMA_STORE
+#define GG_TMA_STORE 1
+#endif
+
 namespace gg {
 
 constexpr int kThreads = 192;  // 6 warps: producer, MMA, 4 x epilogue
@@ -103,8 +107,14 @@ template <int kCG, int kBN, int kAtoms> struct TileCfg {
     static constexpr int kTmemCols = (2 * kBN) <= 32 ? 32 : (2 * kBN) <= 64 ? 64 : (2 * kBN) <= 128 ? 128
                                      : (2 * kBN) <= 256 ? 256 : 512;
     // barriers: full[S], empty[S], tmem_full[2], tmem_empty[2]; then tmem ptr and abort flag
-    static constexpr int kBarOffset = kStages * kStageBytes;
+    // Epilogue staging for TMA stores: per epilogue warp two 32-row x 64-column boxes (4 KB each,
+    // 128-byte swizzle), after the ring.
+    static constexpr int kStageOutBytes = 32 * 64 * 2;
+    static constexpr int kOutOffset = kStages * kStageBytes;
+    static constexpr int kOutBytes = GG_TMA_STORE ? 4 * 2 * kStageOutBytes : 0;
+    static constexpr int kBarOffset = kOutOffset + kOutBytes;
     static constexpr int kSmemBytes = kBarOffset + (2 * kStages + 4) * 8 + 16 + 1024;  // + align slack
+    static_assert(kSmemBytes <= 232448, "over the 227 KB shared-memory limit");
     static_assert(kStages >= 2, "ring too shallow");
     static_assert(kAAtomBytes % 1024 == 0 && kBAtomBytes % 1024 == 0, "swizzle atoms 1024-byte aligned");
 };
@@ -193,6 +203,7 @@ __device__ __forceinline__ uint32_t pack2(uint32_t a, uint32_t b) {
 template <typename T, int kCG, int kBN, int kAtoms>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_sm100(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                       const __grid_constant__ CUtensorMap tmap_out,
                        const __grid_constant__ KernelParams p) {
     using C = TileCfg<kCG, kBN, kAtoms>;
     // Tile N is a launch parameter (multiple of 32, at most kBN): the smem ring and TMEM are sized
@@ -237,6 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         ptx::prefetch_tmap(&tmap_a);
         ptx::prefetch_tmap(&tmap_b);
+        if (GG_TMA_STORE)
+            ptx::prefetch_tmap(&tmap_out);
     }
     if (warp == 1) {
         ptx::tmem_alloc<kCG>(ptx::smem_addr(tmem_ptr_slot), C::kTmemCols);
@@ -384,6 +397,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row_in_cta = q * 32 + int(lane);
         const uint32_t tempty_leader0 = kCG == 2 ? ptx::mapa(tempty_bar(0), 0) : tempty_bar(0);
         T *out = static_cast<T *>(p.out);
+        // this warp's two staging buffers
+        const uint32_t out_stage = smem_base + C::kOutOffset + uint32_t(q) * 2u * C::kStageOutBytes;
+        int out_buf = 0;
         int cursor = 0;
         uint32_t tl = 0;
         for (int u = cluster_id; u < total_units; u += num_clusters, ++tl) {
@@ -436,8 +452,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                         *ctr = 0;  // ready for the next launch
                 }
             }
+            // TMA-store path: the warp's 32 rows all inside the group and no split-K sums; each
+            // pair of 32-column chunks goes out as one 64 x 32 box through a staging buffer.
+            const int slab_rows_ok = m - (tc.mt * C::kClusterM + int(cta_rank) * kBM + q * 32);
+            const int c_tma = (GG_TMA_STORE && splits == 1 && slab_rows_ok >= 32) ? (bn / 64) * 2 : 0;
 #pragma unroll 1
-            for (int c = 0; store_out && c < bn / 32; ++c) {
+            for (int c = 0; c < c_tma; c += 2) {
+                const uint32_t buf = out_stage + uint32_t(out_buf) * C::kStageOutBytes;
+                if (lane == 0)
+                    ptx::bulk_wait_group_read<1>();  // this buffer's previous store has read it
+                __syncwarp();
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t r[32];
+                    ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + hh) * 32), r);
+                    ptx::tmem_wait_ld(r);
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) {
+                        const int j = hh * 4 + jj;  // 16-byte chunk of the 128-byte row
+                        const uint32_t dst = buf + uint32_t(lane) * 128u + uint32_t(((j ^ int(lane & 7u)) * 16));
+                        ptx::st_shared_v4(dst, pack2<T>(r[8 * jj + 0], r[8 * jj + 1]), pack2<T>(r[8 * jj + 2], r[8 * jj + 3]),
+                                          pack2<T>(r[8 * jj + 4], r[8 * jj + 5]), pack2<T>(r[8 * jj + 6], r[8 * jj + 7]));
+                    }
+                }
+                ptx::fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA engine
+                __syncwarp();
+                if (lane == 0) {
+                    ptx::tma_store_2d(&tmap_out, buf, tc.nt * bn + c * 32,
+                                      g_row0 + tc.mt * C::kClusterM + int(cta_rank) * kBM + q * 32);
+                    ptx::bulk_commit_group();
+                }
+                out_buf ^= 1;
+            }
+#pragma unroll 1
+            for (int c = c_tma; store_out && c < bn / 32; ++c) {
                 uint32_t r[32];
                 ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
                 ptx::tmem_wait_ld(r);
@@ -504,6 +552,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ptx::mbar_arrive(tempty_bar(acc));
             }
         }
+        if (GG_TMA_STORE && lane == 0)
+            ptx::bulk_wait_group_all();  // stores complete before the CTA (and its smem) goes away
+        __syncwarp();
     }
 
     // ---------------- teardown ----------------

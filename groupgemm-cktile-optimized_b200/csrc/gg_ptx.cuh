@@ -143,6 +143,24 @@ __device__ __forceinline__ void st_cs_v8(void *p, uint32_t a0, uint32_t a1, uint
                  : "memory");
 }
 
+// ---- TMA stores: shared -> global, tracked in bulk groups of the issuing thread ----
+__device__ __forceinline__ void tma_store_2d(const void *tmap, uint32_t src, int32_t c0, int32_t c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+                 "r"(src), "r"(c0), "r"(c1)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N bulk groups still read their shared-memory source.
+template <int N> __device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until all bulk groups of this thread have completed (writes done).
+__device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
 // ---- Tensor Memory ----
 template <int kCG> __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
     if constexpr (kCG == 1)
