@@ -49,7 +49,23 @@ CONFIGS = {
               desc="P: B=16 experts per GPU, M=1000, N=2880, K=2880, bf16 (BASELINE configs[3])"),
     "T": dict(b=4, m=256, n=512, k=384, dtype="bf16", per_gpu=True,
               desc="T: B=4, M=256, N=512, K=384, bf16 (BASELINE configs[0])"),
+    # E's 131072 tokens routed unevenly (Zipf-like expert popularity, seeded), some experts empty
+    "U": dict(b=256, m=512, n=4096, k=7168, dtype="bf16", per_gpu=False, skew=1.1,
+              desc="U: config E with 131072 tokens over 256 experts routed with Zipf(1.1) popularity (seeded)"),
 }
+
+
+def group_sizes(cfg, g0, g1):
+    """Rows per expert of experts [g0, g1): balanced, or the seeded skewed routing of config U."""
+    if "skew" not in cfg:
+        return [cfg["m"]] * (g1 - g0)
+    total, experts = cfg["m"] * cfg["b"], cfg["b"]
+    rng = np.random.default_rng(2024)
+    weights = 1.0 / np.arange(1, experts + 1) ** cfg["skew"]
+    weights = weights[rng.permutation(experts)]
+    sizes = np.floor(weights / weights.sum() * total).astype(np.int64)
+    sizes[np.argmax(sizes)] += total - sizes.sum()
+    return [int(v) for v in sizes[g0:g1]]
 
 
 def load_package():
@@ -270,8 +286,8 @@ def main():
     total_groups, (g0, g1) = shard_of(cfg, world, rank, gg)
     ng = g1 - g0
     m, n, k = cfg["m"], cfg["n"], cfg["k"]
-    group_m = [m] * ng
-    rows = m * ng
+    group_m = group_sizes(cfg, g0, g1)
+    rows = sum(group_m)
     gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
     x = torch.randn(rows, k, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
     w = torch.empty(ng, n, k, device="cuda", dtype=tdt)
@@ -318,7 +334,7 @@ def main():
         ms_step = float(t.item())
     else:
         ms_step = ms_step_rank
-    total_flops = 2.0 * total_groups * m * n * k
+    total_flops = 2.0 * sum(group_sizes(cfg, 0, total_groups)) * n * k
     value = total_flops / (ms_step * 1e-3) / 1e12
 
     # ---- optional all-gather of the expert outputs (timed separately, not in value) ----

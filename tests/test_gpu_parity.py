@@ -143,6 +143,47 @@ def test_split_k_auto_on_low_tile_count(gg, orc):
     full_case(gg, orc, [512], 4096, 14336, 0)
 
 
+def test_many_tiny_ragged_groups(gg, orc):
+    # 1000 experts with 0..40 tokens each: thousands of partly-filled tiles, many empty groups
+    torch = _torch()
+    rng = np.random.default_rng(7)
+    group_m = [int(v) for v in rng.integers(0, 41, size=1000)]
+    group_m[::7] = [0] * len(group_m[::7])
+    n, k = 128, 192
+    x, w = orc.make_inputs(group_m, n, k, 0)
+    ref = orc.grouped_gemm_f32(x, w, group_m, 0)
+    xd, wd = upload(torch, x), upload(torch, w)
+    for v in (-1, 0, 2):
+        got, detail = run_backend(gg, group_m, n, k, 0, xd, wd, variant=v)
+        bad, mx, first = orc.check16(got, ref, 0)
+        assert bad == 0, (detail, bad, mx, first)
+
+
+def test_run_is_capturable_in_a_cuda_graph(gg, orc):
+    """gg_run is one kernel launch with its arguments fixed at prepare time, so a CUDA graph can
+    capture it and replay it (the launch-bound regime of small problems)."""
+    torch = _torch()
+    group_m, n, k = [256, 100, 0, 300], 512, 384
+    x, w = orc.make_inputs(group_m, n, k, 0)
+    ref = orc.grouped_gemm_f32(x, w, group_m, 0)
+    xd, wd = upload(torch, x), upload(torch, w)
+    out = torch.zeros(sum(group_m) * n, dtype=torch.int16, device="cuda")
+    s = torch.cuda.Stream()
+    b = gg.B200Backend()
+    assert b.prepare(0, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s.cuda_stream) == ""
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(3):
+            b.run(torch.cuda.current_stream().cuda_stream)
+    out.zero_()
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    assert b.device_status(s.cuda_stream) == 0
+    got = out.cpu().numpy().view(np.uint16).reshape(-1, n)
+    assert orc.check16(got, ref, 0)[0] == 0
+
+
 def test_all_groups_empty_is_a_no_op(gg, orc):
     torch = _torch()
     xd = torch.empty(0, dtype=torch.int16, device="cuda")
