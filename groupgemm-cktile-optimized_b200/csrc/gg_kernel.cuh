@@ -399,6 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         T *out = static_cast<T *>(p.out);
         // this warp's two staging buffers
         const uint32_t out_stage = smem_base + C::kOutOffset + uint32_t(q) * 2u * C::kStageOutBytes;
+        const uint64_t store_policy = ptx::l2_policy_evict_first();  // out is never re-read here
         int out_buf = 0;
         int cursor = 0;
         uint32_t tl = 0;
@@ -479,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) {
                     ptx::tma_store_2d(&tmap_out, buf, tc.nt * bn + c * 32,
-                                      g_row0 + tc.mt * C::kClusterM + int(cta_rank) * kBM + q * 32);
+                                      g_row0 + tc.mt * C::kClusterM + int(cta_rank) * kBM + q * 32, store_policy);
                     ptx::bulk_commit_group();
                 }
                 out_buf ^= 1;

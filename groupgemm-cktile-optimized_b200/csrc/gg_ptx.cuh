@@ -144,9 +144,17 @@ __device__ __forceinline__ void st_cs_v8(void *p, uint32_t a0, uint32_t a1, uint
 }
 
 // ---- TMA stores: shared -> global, tracked in bulk groups of the issuing thread ----
-__device__ __forceinline__ void tma_store_2d(const void *tmap, uint32_t src, int32_t c0, int32_t c1) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
-                 "r"(src), "r"(c0), "r"(c1)
+// L2 cache policy: evict first (data that is written once and not re-read by this kernel).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ void tma_store_2d(const void *tmap, uint32_t src, int32_t c0, int32_t c1, uint64_t policy) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+                     tmap),
+                 "r"(src), "r"(c0), "r"(c1), "l"(policy)
                  : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
