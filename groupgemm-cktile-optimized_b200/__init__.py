@@ -40,6 +40,25 @@ class GGProblem(ctypes.Structure):
     ]
 
 
+# Backward operations accepted by B200Backend.prepare_grad (enum gg_op).
+OP_FORWARD, OP_DGRAD, OP_WGRAD = 0, 1, 2
+
+
+class GGGradProblem(ctypes.Structure):
+    _fields_ = [
+        ("dtype", ctypes.c_int32),
+        ("group_num", ctypes.c_int32),
+        ("n", ctypes.c_int64),
+        ("k", ctypes.c_int64),
+        ("group_m", ctypes.POINTER(ctypes.c_int64)),
+        ("dy", ctypes.c_void_p),
+        ("x", ctypes.c_void_p),
+        ("w", ctypes.c_void_p),
+        ("dx", ctypes.c_void_p),
+        ("dw", ctypes.c_void_p),
+    ]
+
+
 # Every symbol include/gg_b200.h declares, with its ctypes signature.
 SIGNATURES = {
     "gg_abi_version": (ctypes.c_int, []),
@@ -47,6 +66,8 @@ SIGNATURES = {
     "gg_name": (ctypes.c_char_p, [ctypes.c_void_p]),
     "gg_prepare": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(GGProblem), ctypes.c_void_p,
                                   ctypes.c_char_p, ctypes.c_size_t]),
+    "gg_prepare_grad": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(GGGradProblem), ctypes.c_int32,
+                                       ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]),
     "gg_run": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "gg_release": (None, [ctypes.c_void_p]),
     "gg_detail": (ctypes.c_char_p, [ctypes.c_void_p]),
@@ -130,6 +151,24 @@ class B200Backend:
                          ctypes.c_void_p(w_ptr or None), ctypes.c_void_p(out_ptr or None))
         why = ctypes.create_string_buffer(256)
         rc = self._lib.gg_prepare(self._h, ctypes.byref(prob), ctypes.c_void_p(stream or None), why, 256)
+        if rc == GG_OK:
+            return ""
+        if rc == GG_NOT_SUPPORTED:
+            return why.value.decode() or "not supported"
+        raise GGError(rc, self.last_error())
+
+    def prepare_grad(self, op: int, dtype: int, group_m: Sequence[int], n: int, k: int, dy_ptr: int = 0,
+                     x_ptr: int = 0, w_ptr: int = 0, dx_ptr: int = 0, dw_ptr: int = 0, stream: int = 0) -> str:
+        """Prepare a backward grouped GEMM: OP_DGRAD (dx = dy @ w[g], needs dy, w, dx) or OP_WGRAD
+        (dw[g] = dy[g]^T @ x[g], needs dy, x, dw). Then run() launches it. Returns "" or the N/A
+        reason; raises GGError on a CUDA or argument error."""
+        gm = (ctypes.c_int64 * len(group_m))(*[int(m) for m in group_m])
+        self._group_m = gm
+        vp = lambda v: ctypes.c_void_p(v or None)  # noqa: E731
+        prob = GGGradProblem(int(dtype), len(group_m), int(n), int(k), gm, vp(dy_ptr), vp(x_ptr), vp(w_ptr),
+                             vp(dx_ptr), vp(dw_ptr))
+        why = ctypes.create_string_buffer(256)
+        rc = self._lib.gg_prepare_grad(self._h, ctypes.byref(prob), int(op), vp(stream), why, 256)
         if rc == GG_OK:
             return ""
         if rc == GG_NOT_SUPPORTED:

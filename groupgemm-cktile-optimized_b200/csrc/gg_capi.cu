@@ -49,28 +49,29 @@ EncodeTiledFn get_encode_fn() {
     return fn;
 }
 
-// One compiled instance of the kernel.
+// One compiled instance of the kernel: a tile shape, for each operation and dtype.
 struct Variant {
     int cg;        // CTAs per tile (1 or 2)
     int bn;        // tile N
     int cluster_m; // tile M
     int stages;
     int smem;
-    const void *fn_bf16;
-    const void *fn_fp16;
+    const void *fn[3][2];  // [operation: forward, dgrad, wgrad][dtype: bf16, fp16]
     int atoms;     // 64-element K atoms per stage
 };
 
+template <int kCG, int kBN, int kAtoms, int kOp> void set_fns(Variant &v) {
+    v.fn[kOp][GG_BF16] = reinterpret_cast<const void *>(&gg::grouped_gemm_sm100<__nv_bfloat16, kCG, kBN, kAtoms, kOp>);
+    v.fn[kOp][GG_FP16] = reinterpret_cast<const void *>(&gg::grouped_gemm_sm100<__half, kCG, kBN, kAtoms, kOp>);
+}
+
 template <int kCG, int kBN, int kAtoms> Variant make_variant() {
     using C = gg::TileCfg<kCG, kBN, kAtoms>;
-    return Variant{kCG,
-                   kBN,
-                   C::kClusterM,
-                   C::kStages,
-                   C::kSmemBytes,
-                   reinterpret_cast<const void *>(&gg::grouped_gemm_sm100<__nv_bfloat16, kCG, kBN, kAtoms>),
-                   reinterpret_cast<const void *>(&gg::grouped_gemm_sm100<__half, kCG, kBN, kAtoms>),
-                   kAtoms};
+    Variant v{kCG, kBN, C::kClusterM, C::kStages, C::kSmemBytes, {}, kAtoms};
+    set_fns<kCG, kBN, kAtoms, gg::kOpForward>(v);
+    set_fns<kCG, kBN, kAtoms, gg::kOpDgrad>(v);
+    set_fns<kCG, kBN, kAtoms, gg::kOpWgrad>(v);
+    return v;
 }
 
 const Variant &variant_at(int i) {
@@ -105,6 +106,9 @@ struct gg_handle {
     size_t ws_cap = 0;      // bytes
     int32_t *d_counters = nullptr;
     size_t counters_cap = 0;  // bytes
+    CUtensorMap *d_gmaps = nullptr;  // wgrad: per-group tensor maps
+    size_t gmaps_cap = 0;            // maps
+    int op = 0;                      // gg::kOpForward / kOpDgrad / kOpWgrad
     CUtensorMap tmap_a{}, tmap_b{}, tmap_out{};
     gg::KernelParams params{};
     int grid = 0;
@@ -187,7 +191,7 @@ double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots_pai
 // `forced_bn` > 0 restrict the search. `pairs` is the number of co-resident CTA pairs of the
 // 2-CTA variant.
 Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_variant, int forced_bn,
-                     int max_splits = 1) {
+                     int max_splits = 1, bool mn_major_b = false) {
     Choice best{-1, 0, 1};
     double best_t = 0;
     const int64_t atoms = (p->k + gg::kBK - 1) / gg::kBK;
@@ -203,6 +207,8 @@ Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_var
                 continue;
             if (forced_bn <= 0 && bn < 128)
                 continue;  // narrower tiles are issue-bound; only on request
+            if (mn_major_b && (bn / v.cg) % 64 != 0)
+                continue;  // MN-major B is loaded in 64-column boxes
             const int64_t tiles = tiles_for(p, v, bn);
             for (int s = 1; s <= max_splits; ++s) {
                 // split only below one full wave, and only with >= 8 K atoms per split
@@ -283,6 +289,10 @@ void gg_release(gg_handle *h) {
         cudaFree(h->d_ws);
     if (h->d_counters)
         cudaFree(h->d_counters);
+    if (h->d_gmaps)
+        cudaFree(h->d_gmaps);
+    h->d_gmaps = nullptr;
+    h->gmaps_cap = 0;
     h->d_meta = nullptr;
     h->d_status = nullptr;
     h->d_ws = nullptr;
@@ -310,46 +320,109 @@ int gg_expert_shard(int32_t group_num, int32_t world, int32_t rank, int32_t *g0,
     return GG_OK;
 }
 
-int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why, size_t why_len) {
-    if (!h)
-        return GG_ERR_ARG;
-    h->ready = false;
-    h->last_error.clear();
-    if (why && why_len)
-        why[0] = '\0';
-    if (!p)
-        return fail(h, GG_ERR_ARG, "null problem");
+}  // extern "C"
 
+namespace {
+
+// One grouped GEMM of the layer, in the kernel's terms: A rows x B columns over a reduction.
+//   forward: a = x,  b = w, out = out [sum(M), n]  (reduction k)
+//   dgrad:   a = dy, b = w, out = dx  [sum(M), k]  (reduction n)
+//   wgrad:   a = dy, b = x, out = dw  [G*n, k]     (reduction: the group's tokens)
+struct OpProblem {
+    int op;
+    int32_t dtype;
+    int32_t group_num;
+    int64_t n, k;  // the layer's N and K
+    const int64_t *group_m;
+    const void *a, *b;
+    void *out;
+};
+
+const char *op_name(int op) { return op == gg::kOpDgrad ? "dgrad" : op == gg::kOpWgrad ? "wgrad" : "forward"; }
+
+int encode_2d(EncodeTiledFn encode, CUtensorMap *m, CUtensorMapDataType dt, const void *base, int64_t cols,
+              int64_t rows, uint32_t box_cols, uint32_t box_rows, CUtensorMapL2promotion promo) {
+    const cuuint64_t dim[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+    const cuuint64_t stride[1] = {cuuint64_t(cols) * 2};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estride[2] = {1, 1};
+    return int(encode(m, dt, 2, const_cast<void *>(base), dim, stride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
+}
+
+// w [G, n, k] as a 3-D map (k, n, G): a box never crosses into the next expert.
+int encode_w(EncodeTiledFn encode, CUtensorMap *m, CUtensorMapDataType dt, const void *w, int64_t n, int64_t k,
+             int64_t G, uint32_t box_k, uint32_t box_n) {
+    const cuuint64_t dim[3] = {cuuint64_t(k), cuuint64_t(n), cuuint64_t(G)};
+    const cuuint64_t stride[2] = {cuuint64_t(k) * 2, cuuint64_t(n) * cuuint64_t(k) * 2};
+    const cuuint32_t box[3] = {box_k, box_n, 1};
+    const cuuint32_t estride[3] = {1, 1, 1};
+    return int(encode(m, dt, 3, const_cast<void *>(w), dim, stride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
+}
+
+int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, size_t why_len) {
+    const int op = q.op;
     // ---- argument checks (host only; an unsupported shape is an N/A, not an error) ----
-    if (p->dtype != GG_BF16 && p->dtype != GG_FP16)
+    if (q.dtype != GG_BF16 && q.dtype != GG_FP16)
         return refuse(h, why, why_len, "dtype must be bf16 (0) or fp16 (1)");
-    if (p->group_num < 1)
+    if (q.group_num < 1)
         return refuse(h, why, why_len, "group_num must be >= 1");
-    if (!p->group_m)
+    if (!q.group_m)
         return refuse(h, why, why_len, "group_m is null");
-    if (p->n < 1 || p->k < 1)
+    if (q.n < 1 || q.k < 1)
         return refuse(h, why, why_len, "n and k must be >= 1");
-    if (p->k % 8 != 0)
+    if (q.k % 8 != 0)
         return refuse(h, why, why_len, "k must be a multiple of 8 (16-byte TMA row stride)");
-    if (p->n % 8 != 0)
+    if (q.n % 8 != 0)
         return refuse(h, why, why_len, "n must be a multiple of 8 (16-byte output row stride)");
-    if (p->n > (int64_t(1) << 30) || p->k > (int64_t(1) << 30))
+    if (q.n > (int64_t(1) << 30) || q.k > (int64_t(1) << 30))
         return refuse(h, why, why_len, "n and k must be below 2^30");
     int64_t total_m = 0;
-    for (int g = 0; g < p->group_num; ++g) {
-        if (p->group_m[g] < 0)
+    for (int g = 0; g < q.group_num; ++g) {
+        if (q.group_m[g] < 0)
             return refuse(h, why, why_len, "group_m entries must be >= 0");
-        total_m += p->group_m[g];
+        total_m += q.group_m[g];
         if (total_m >= (int64_t(1) << 31))
             return refuse(h, why, why_len, "sum(group_m) must be below 2^31");
     }
-    if (total_m > 0 && (!p->x || !p->w || !p->out))
-        return refuse(h, why, why_len, "x, w and out must be non-null device pointers");
-    if ((reinterpret_cast<uintptr_t>(p->x) | reinterpret_cast<uintptr_t>(p->w) |
-         reinterpret_cast<uintptr_t>(p->out)) & 15u)
-        return refuse(h, why, why_len, "x, w and out must be 16-byte aligned");
-    if (int64_t(p->group_num) * p->n * p->k >= (int64_t(1) << 40) / 2)
+    if (op == gg::kOpForward) {
+        if (total_m > 0 && (!q.a || !q.b || !q.out))
+            return refuse(h, why, why_len, "x, w and out must be non-null device pointers");
+        if ((reinterpret_cast<uintptr_t>(q.a) | reinterpret_cast<uintptr_t>(q.b) | reinterpret_cast<uintptr_t>(q.out)) &
+            15u)
+            return refuse(h, why, why_len, "x, w and out must be 16-byte aligned");
+    } else {
+        const char *names = op == gg::kOpDgrad ? "dy, w and dx" : "dy, x and dw";
+        char msg[96];
+        if ((total_m > 0 && (!q.a || !q.b)) || ((total_m > 0 || op == gg::kOpWgrad) && !q.out)) {
+            std::snprintf(msg, sizeof(msg), "%s must be non-null device pointers", names);
+            return refuse(h, why, why_len, msg);
+        }
+        if ((reinterpret_cast<uintptr_t>(q.a) | reinterpret_cast<uintptr_t>(q.b) | reinterpret_cast<uintptr_t>(q.out)) &
+            15u) {
+            std::snprintf(msg, sizeof(msg), "%s must be 16-byte aligned", names);
+            return refuse(h, why, why_len, msg);
+        }
+    }
+    if (int64_t(q.group_num) * q.n * q.k >= (int64_t(1) << 40) / 2)
         return refuse(h, why, why_len, "weight tensor too large for one TMA descriptor");
+    if (op == gg::kOpWgrad && int64_t(q.group_num) * q.n >= (int64_t(1) << 31))
+        return refuse(h, why, why_len, "group_num * n must be below 2^31 for wgrad");
+    if (op == gg::kOpWgrad && h->opt_split > 1)
+        return refuse(h, why, why_len, "split-K is not available for wgrad (per-group reduction lengths)");
+
+    // The problem as the cost model sees it: rows per group, output columns, reduction length.
+    const int G = q.group_num;
+    const int64_t out_cols = op == gg::kOpForward ? q.n : q.k;
+    std::vector<int64_t> wrows;
+    gg_problem cm{q.dtype, G, out_cols, op == gg::kOpForward ? q.k : q.n, q.group_m, q.a, q.b, q.out};
+    if (op == gg::kOpWgrad) {
+        wrows.assign(size_t(G), q.n);
+        cm.group_m = wrows.data();
+        cm.k = std::max<int64_t>(8, (total_m + G - 1) / G);  // mean tokens per expert
+    }
+    const bool mn_b = op != gg::kOpForward;
 
     // ---- device + variant ----
     int dev = 0;
@@ -368,7 +441,7 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     int pairs = 0;
     {
         const Variant &v0 = variant_at(0);
-        const void *fn0 = p->dtype == GG_BF16 ? v0.fn_bf16 : v0.fn_fp16;
+        const void *fn0 = v0.fn[op][q.dtype];
         GG_CUDA(h, cudaFuncSetAttribute(fn0, cudaFuncAttributeMaxDynamicSharedMemorySize, v0.smem));
         cudaLaunchConfig_t cfg{};
         cudaLaunchAttribute attr[1];
@@ -389,35 +462,39 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     }
     if (h->opt_bn > 0 && h->opt_variant >= 0 && h->opt_bn > variant_at(h->opt_variant).bn)
         return refuse(h, why, why_len, "bn is wider than the variant's tile");
-    // split-K candidates: auto (up to 4) unless forced; never when the fp32 partials would be large
+    // split-K candidates: auto (up to 4) unless forced; never when the fp32 partials would be
+    // large; wgrad never splits
     int max_splits = h->opt_split > 0 ? h->opt_split : 4;
-    if (double(total_m) * double(p->n) * 4.0 * max_splits > 512.0 * (1 << 20))
+    if (double(total_m) * double(out_cols) * 4.0 * max_splits > 512.0 * (1 << 20))
         max_splits = h->opt_split > 0 ? h->opt_split : 1;
-    Choice ch = choose_tiling(p, num_sms, pairs, h->opt_variant, h->opt_bn, max_splits);
-    if (h->opt_split > 0 && ch.variant >= 0) {
+    if (op == gg::kOpWgrad)
+        max_splits = 1;
+    Choice ch = choose_tiling(&cm, num_sms, pairs, h->opt_variant, h->opt_bn, max_splits, mn_b);
+    if (h->opt_split > 0 && ch.variant >= 0 && op != gg::kOpWgrad) {
         // forced split count: keep the chosen tiling, use exactly that many splits
-        const int64_t atoms = (p->k + gg::kBK - 1) / gg::kBK;
+        const int64_t atoms = (cm.k + gg::kBK - 1) / gg::kBK;
         if (h->opt_split > atoms)
             return refuse(h, why, why_len, "split exceeds the number of 64-wide K atoms");
         ch.splits = h->opt_split;
     }
     if (ch.variant < 0)
-        return refuse(h, why, why_len, "no kernel variant fits this device and these options");
+        return refuse(h, why, why_len,
+                      mn_b && h->opt_bn > 0 ? "bn must be a multiple of 64 per CTA for a backward operation"
+                                            : "no kernel variant fits this device and these options");
     const int vi = ch.variant;
     const int bn = ch.bn;
     const Variant &v = variant_at(vi);
-    const void *fn = p->dtype == GG_BF16 ? v.fn_bf16 : v.fn_fp16;
+    const void *fn = v.fn[op][q.dtype];
 
-    // ---- group arguments: tile offsets (this tiling) and row offsets ----
-    const int G = p->group_num;
-    const int64_t tiles_n = (p->n + bn - 1) / bn;
+    // ---- group arguments: tile offsets (this tiling) and row (token) offsets ----
+    const int64_t tiles_n = (out_cols + bn - 1) / bn;
     std::vector<int32_t> meta(2 * size_t(G + 1));
     int64_t tiles = 0, rows = 0;
     for (int g = 0; g < G; ++g) {
         meta[g] = int32_t(tiles);
         meta[G + 1 + g] = int32_t(rows);
-        tiles += (p->group_m[g] + v.cluster_m - 1) / v.cluster_m * tiles_n;
-        rows += p->group_m[g];
+        tiles += (cm.group_m[g] + v.cluster_m - 1) / v.cluster_m * tiles_n;
+        rows += q.group_m[g];
         if (tiles >= (int64_t(1) << 31))
             return refuse(h, why, why_len, "too many tiles");
     }
@@ -436,7 +513,7 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
         GG_CUDA(h, cudaMalloc(&h->d_status, 16));
     GG_CUDA(h, cudaMemsetAsync(h->d_status, 0, 16, stream));
     if (ch.splits > 1) {
-        const size_t ws_bytes = size_t(ch.splits) * size_t(total_m) * size_t(p->n) * sizeof(float);
+        const size_t ws_bytes = size_t(ch.splits) * size_t(total_m) * size_t(out_cols) * sizeof(float);
         const size_t ctr_bytes = size_t(tiles) * size_t(v.cg) * 4 * sizeof(int32_t);
         if (h->ws_cap < ws_bytes) {
             if (h->d_ws)
@@ -461,33 +538,56 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
 
     // ---- TMA descriptors ----
     const CUtensorMapDataType dt =
-        p->dtype == GG_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    if (total_m > 0) {
-        const cuuint64_t a_dim[2] = {cuuint64_t(p->k), cuuint64_t(total_m)};
-        const cuuint64_t a_stride[1] = {cuuint64_t(p->k) * 2};
-        const cuuint32_t a_box[2] = {gg::kBK, gg::kBM};
-        const cuuint32_t estride[3] = {1, 1, 1};
-        CUresult r = encode(&h->tmap_a, dt, 2, const_cast<void *>(p->x), a_dim, a_stride, a_box, estride,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS)
-            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed: %d", int(r));
-        const cuuint64_t b_dim[3] = {cuuint64_t(p->k), cuuint64_t(p->n), cuuint64_t(G)};
-        const cuuint64_t b_stride[2] = {cuuint64_t(p->k) * 2, cuuint64_t(p->n) * cuuint64_t(p->k) * 2};
-        const cuuint32_t b_box[3] = {gg::kBK, cuuint32_t(bn / v.cg), 1};
-        r = encode(&h->tmap_b, dt, 3, const_cast<void *>(p->w), b_dim, b_stride, b_box, estride,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS)
-            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(w) failed: %d", int(r));
+        q.dtype == GG_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint32_t b_box = uint32_t(bn / v.cg);
+    h->tmap_a = CUtensorMap{};
+    h->tmap_b = CUtensorMap{};
+    h->tmap_out = CUtensorMap{};
+    std::vector<CUtensorMap> gmaps;
+    if (op == gg::kOpForward && total_m > 0) {
+        if (encode_2d(encode, &h->tmap_a, dt, q.a, q.k, total_m, gg::kBK, gg::kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed");
+        if (encode_w(encode, &h->tmap_b, dt, q.b, q.n, q.k, G, gg::kBK, b_box))
+            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(w) failed");
         // out [sum(M), N]: the epilogue's TMA stores, 32 rows x 64 columns per box
-        const cuuint64_t o_dim[2] = {cuuint64_t(p->n), cuuint64_t(total_m)};
-        const cuuint64_t o_stride[1] = {cuuint64_t(p->n) * 2};
-        const cuuint32_t o_box[2] = {64, 32};
-        r = encode(&h->tmap_out, dt, 2, p->out, o_dim, o_stride, o_box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS)
-            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(out) failed: %d", int(r));
+        if (encode_2d(encode, &h->tmap_out, dt, q.out, q.n, total_m, 64, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE))
+            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(out) failed");
+    } else if (op == gg::kOpDgrad && total_m > 0) {
+        // A = dy [sum(M), N], K-major over N; B = w[g] read as 64 (K) x 64 (N) MN-major boxes
+        if (encode_2d(encode, &h->tmap_a, dt, q.a, q.n, total_m, gg::kBK, gg::kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(dy) failed");
+        if (encode_w(encode, &h->tmap_b, dt, q.b, q.n, q.k, G, 64, gg::kBK))
+            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(w) failed");
+        if (encode_2d(encode, &h->tmap_out, dt, q.out, q.k, total_m, 64, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE))
+            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(dx) failed");
+    } else if (op == gg::kOpWgrad) {
+        // Per group: dy rows and x rows of the group's tokens, each bounded by the group so that the
+        // token tail reads zeros; 64 x 64 MN-major boxes. An empty group's maps are never read.
+        gmaps.assign(2 * size_t(G), CUtensorMap{});
+        int64_t r0 = 0;
+        for (int g = 0; g < G; ++g) {
+            const int64_t m = q.group_m[g];
+            if (m > 0) {
+                const char *dy = static_cast<const char *>(q.a) + r0 * q.n * 2;
+                const char *x = static_cast<const char *>(q.b) + r0 * q.k * 2;
+                if (encode_2d(encode, &gmaps[2 * g], dt, dy, q.n, m, 64, gg::kBK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B) ||
+                    encode_2d(encode, &gmaps[2 * g + 1], dt, x, q.k, m, 64, gg::kBK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+                    return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(group %d) failed", g);
+            }
+            r0 += m;
+        }
+        if (encode_2d(encode, &h->tmap_out, dt, q.out, q.k, int64_t(G) * q.n, 64, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE))
+            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(dw) failed");
+        if (h->gmaps_cap < gmaps.size()) {
+            if (h->d_gmaps)
+                cudaFree(h->d_gmaps);
+            h->d_gmaps = nullptr;
+            h->gmaps_cap = 0;
+            GG_CUDA(h, cudaMalloc(&h->d_gmaps, gmaps.size() * sizeof(CUtensorMap)));
+            h->gmaps_cap = gmaps.size();
+        }
+        GG_CUDA(h, cudaMemcpyAsync(h->d_gmaps, gmaps.data(), gmaps.size() * sizeof(CUtensorMap),
+                                   cudaMemcpyHostToDevice, stream));
     }
 
     // ---- raster band and persistent grid ----
@@ -504,21 +604,24 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     h->grid = int(std::max<int64_t>(v.cg, std::min<int64_t>(slots, want)));
 
     gg::KernelParams &kp = h->params;
+    kp = gg::KernelParams{};
     kp.tile_off = h->d_meta;
     kp.row_off = h->d_meta + (G + 1);
-    kp.out = p->out;
+    kp.out = q.out;
     kp.status = h->d_status;
+    kp.gmaps = op == gg::kOpWgrad ? h->d_gmaps : nullptr;
     kp.group_num = G;
-    kp.n = int32_t(p->n);
-    kp.k = int32_t(p->k);
-    kp.num_kb = int32_t((p->k + gg::kBK - 1) / gg::kBK);
+    kp.n = int32_t(out_cols);
+    kp.k = int32_t(op == gg::kOpForward ? q.k : q.n);
+    kp.tile_rows = op == gg::kOpWgrad ? int32_t(q.n) : 0;
+    kp.num_kb = int32_t((kp.k + gg::kBK - 1) / gg::kBK);
     kp.tiles_n = int32_t(tiles_n);
     kp.bn = bn;
     kp.total_tiles = int32_t(tiles);
     kp.splits = ch.splits;
     kp.ws = ch.splits > 1 ? h->d_ws : nullptr;
     kp.counters = ch.splits > 1 ? h->d_counters : nullptr;
-    kp.ws_stride = total_m * p->n;
+    kp.ws_stride = total_m * out_cols;
     kp.band = band;
     kp.test_stall = h->opt_test_stall;
     kp.timeout_ns = uint64_t(h->opt_timeout_ms) * 1000000ull;
@@ -526,7 +629,8 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     GG_CUDA(h, cudaStreamSynchronize(stream));
 
     h->device = dev;
-    h->dtype = p->dtype;
+    h->dtype = q.dtype;
+    h->op = op;
     h->variant = vi;
     h->total_m = total_m;
     h->fn = fn;
@@ -534,12 +638,50 @@ int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why,
     h->cg = v.cg;
     char d[256];
     std::snprintf(d, sizeof(d),
-                  "gg_sm100<%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld split=%d grid=%d band=%d",
-                  p->dtype == GG_BF16 ? "bf16" : "fp16", v.cluster_m, bn, gg::kBK * v.atoms, v.cg, v.stages,
-                  (long long)tiles, ch.splits, h->grid, band);
+                  "gg_sm100<%s%s%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld split=%d grid=%d band=%d",
+                  q.dtype == GG_BF16 ? "bf16" : "fp16", op == gg::kOpForward ? "" : ",", op == gg::kOpForward ? "" : op_name(op),
+                  v.cluster_m, bn, gg::kBK * v.atoms, v.cg, v.stages, (long long)tiles, ch.splits, h->grid, band);
     h->detail = d;
     h->ready = true;
     return GG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why, size_t why_len) {
+    if (!h)
+        return GG_ERR_ARG;
+    h->ready = false;
+    h->last_error.clear();
+    if (why && why_len)
+        why[0] = '\0';
+    if (!p)
+        return fail(h, GG_ERR_ARG, "null problem");
+    const OpProblem q{gg::kOpForward, p->dtype, p->group_num, p->n, p->k, p->group_m, p->x, p->w, p->out};
+    return prepare_op(h, q, stream, why, why_len);
+}
+
+int gg_prepare_grad(gg_handle *h, const gg_grad_problem *p, int32_t op, gg_stream_t stream, char *why,
+                    size_t why_len) {
+    if (!h)
+        return GG_ERR_ARG;
+    h->ready = false;
+    h->last_error.clear();
+    if (why && why_len)
+        why[0] = '\0';
+    if (!p)
+        return fail(h, GG_ERR_ARG, "null problem");
+    if (op == GG_OP_DGRAD) {
+        const OpProblem q{gg::kOpDgrad, p->dtype, p->group_num, p->n, p->k, p->group_m, p->dy, p->w, p->dx};
+        return prepare_op(h, q, stream, why, why_len);
+    }
+    if (op == GG_OP_WGRAD) {
+        const OpProblem q{gg::kOpWgrad, p->dtype, p->group_num, p->n, p->k, p->group_m, p->dy, p->x, p->dw};
+        return prepare_op(h, q, stream, why, why_len);
+    }
+    return fail(h, GG_ERR_ARG, "op must be GG_OP_DGRAD (1) or GG_OP_WGRAD (2)");
 }
 
 int gg_run(gg_handle *h, gg_stream_t stream) {
@@ -641,7 +783,7 @@ cudaError_t noalloc_device_setup(int dev, NoAllocDevice &d) {
         return e;
     for (int i = 0; i < kNumVariants; ++i) {
         const Variant &v = variant_at(i);
-        for (const void *fn : {v.fn_bf16, v.fn_fp16})
+        for (const void *fn : {v.fn[gg::kOpForward][GG_BF16], v.fn[gg::kOpForward][GG_FP16]})
             if ((e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem)) != cudaSuccess)
                 return e;
     }
@@ -657,7 +799,7 @@ cudaError_t noalloc_device_setup(int dev, NoAllocDevice &d) {
     cfg.dynamicSmemBytes = size_t(v0.smem);
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if ((e = cudaOccupancyMaxActiveClusters(&d.clusters_v0, v0.fn_bf16, &cfg)) != cudaSuccess)
+    if ((e = cudaOccupancyMaxActiveClusters(&d.clusters_v0, v0.fn[gg::kOpForward][GG_BF16], &cfg)) != cudaSuccess)
         return e;
     d.ready = true;
     return cudaSuccess;
@@ -854,7 +996,7 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     void *args[4] = {&tmap_a, &tmap_b, &tmap_out, &kp};
-    if ((e = cudaLaunchKernelExC(&cfg, p->dtype == GG_BF16 ? v.fn_bf16 : v.fn_fp16, args)) != cudaSuccess)
+    if ((e = cudaLaunchKernelExC(&cfg, v.fn[gg::kOpForward][p->dtype], args)) != cudaSuccess)
         return cuda_fail("kernel launch", e);
 
     if (status_out) {

@@ -30,6 +30,22 @@
 //
 // Every wait is bounded. A wait that runs out sets a device status word (role and barrier)
 // and all roles leave their loops; the kernel then frees its Tensor Memory and returns.
+//
+// The same kernel, instantiated per operation (kOp), computes the two backward grouped GEMMs of
+// the MoE layer (the transA / non-transA calls of the reference's vendored Primus-Turbo grouped
+// GEMM, third_party/primus_turbo/kernels/hipblaslt_grouped_gemm.cu:80-96,199-240):
+//
+//   dgrad: dx[rows of g] = dy[rows of g] @ w[g]      dy [sum(M), N] (A, K-major over N),
+//                                                    w[g] [N, K] (B, MN-major), dx [sum(M), K]
+//   wgrad: dw[g] = dy[rows of g]^T @ x[rows of g]    dy^T (A, MN-major), x (B, MN-major),
+//                                                    dw [G, N, K]; the reduction runs over the
+//                                                    group's tokens, an expert without tokens
+//                                                    gets dw[g] = 0
+//
+// MN-major operands are loaded as 64-wide boxes (one 128-byte swizzle row each) and described to
+// the tensor core with MN-major shared-memory descriptors; no transpose pass is needed. For wgrad
+// the K tail of every group (tokens past the group's last row) must read zeros, so each group has
+// its own pair of tensor maps, bounded by the group's rows, in global memory.
 #pragma once
 
 #include <cuda.h>
@@ -60,15 +76,20 @@ enum : uint32_t {
     kRoleEpilogue = 3u << 8,
 };
 
+// Operation computed by one instance of the kernel.
+enum : int { kOpForward = 0, kOpDgrad = 1, kOpWgrad = 2 };
+
 struct KernelParams {
     const int32_t *tile_off;  // [G+1] first tile of each group (cluster tiles)
-    const int32_t *row_off;   // [G+1] first row of each group in x / out
+    const int32_t *row_off;   // [G+1] first row (token) of each group in x / dy / out / dx
     void *out;
     uint32_t *status;
+    const CUtensorMap *gmaps;  // wgrad: [2G] per-group maps (A = dy rows of g, B = x rows of g)
     int32_t group_num;
-    int32_t n;
-    int32_t k;
-    int32_t num_kb;       // ceil(K / 64): K atoms
+    int32_t n;            // output columns: N (forward), K (dgrad, wgrad)
+    int32_t k;            // reduction extent: K (forward), N (dgrad); unused by wgrad
+    int32_t tile_rows;    // wgrad: output rows per group (N)
+    int32_t num_kb;       // ceil(reduction / 64): K atoms (forward, dgrad)
     int32_t tiles_n;      // ceil(N / bn)
     int32_t bn;           // tile N of this launch: a multiple of 32, <= the variant's kBN
     int32_t total_tiles;  // tile_off[G]
@@ -121,6 +142,9 @@ template <int kCG, int kBN, int kAtoms> struct TileCfg {
 
 struct TileCoord {
     int g, mt, nt;
+    int rows;          // output rows of the group (tokens for forward/dgrad, N for wgrad)
+    int out_row0;      // first output row of the group
+    int red_atoms;     // 64-wide reduction atoms of the group
 };
 
 // Map a linear tile index to (group, m-tile, n-tile). Within a group, tiles are rastered in
@@ -128,21 +152,32 @@ struct TileCoord {
 // running tiles share one weight panel (n-tile) and the band's activation rows stay in L2 —
 // the role CK's GemmSpatiallyLocalTilePartitioner<8,4> plays in the reference
 // (ck_kernel/ck_grouped_gemm_config.hpp:74-77).
-template <int kClusterM>
+template <int kClusterM, int kOp>
 __device__ __forceinline__ TileCoord decode_tile(const KernelParams &p, int t, int &cursor) {
     while (__ldg(&p.tile_off[cursor + 1]) <= t)
         ++cursor;
-    const int g = cursor;
-    const int local = t - __ldg(&p.tile_off[g]);
-    const int m = __ldg(&p.row_off[g + 1]) - __ldg(&p.row_off[g]);
-    const int tiles_m = (m + kClusterM - 1) / kClusterM;
+    TileCoord tc;
+    tc.g = cursor;
+    const int local = t - __ldg(&p.tile_off[tc.g]);
+    const int r0 = __ldg(&p.row_off[tc.g]);
+    const int m = __ldg(&p.row_off[tc.g + 1]) - r0;
+    if constexpr (kOp == kOpWgrad) {
+        tc.rows = p.tile_rows;
+        tc.out_row0 = tc.g * p.tile_rows;
+        tc.red_atoms = (m + kBK - 1) / kBK;
+    } else {
+        tc.rows = m;
+        tc.out_row0 = r0;
+        tc.red_atoms = p.num_kb;
+    }
+    const int tiles_m = (tc.rows + kClusterM - 1) / kClusterM;
     const int band_tiles = p.band * p.tiles_n;
     const int b = local / band_tiles;
     const int r = local - b * band_tiles;
     const int rows = min(p.band, tiles_m - b * p.band);
-    const int nt = r / rows;
-    const int mt = b * p.band + (r - nt * rows);
-    return {g, mt, nt};
+    tc.nt = r / rows;
+    tc.mt = b * p.band + (r - tc.nt * rows);
+    return tc;
 }
 
 struct Abort {
@@ -200,18 +235,40 @@ __device__ __forceinline__ uint32_t pack2(uint32_t a, uint32_t b) {
     }
 }
 
-template <typename T, int kCG, int kBN, int kAtoms>
+// Issue one 2-D / 3-D TMA load into this CTA's shared memory, completing on `bar` (in a CTA pair
+// the leader's barrier, through the .cta_group::2 form).
+template <int kCG>
+__device__ __forceinline__ void load_2d(uint32_t dst, const void *map, uint32_t bar, int c0, int c1) {
+    if constexpr (kCG == 1)
+        ptx::tma_load_2d(dst, map, bar, c0, c1);
+    else
+        ptx::tma_load_2d_pair(dst, map, bar, c0, c1);
+}
+template <int kCG>
+__device__ __forceinline__ void load_3d(uint32_t dst, const void *map, uint32_t bar, int c0, int c1, int c2) {
+    if constexpr (kCG == 1)
+        ptx::tma_load_3d(dst, map, bar, c0, c1, c2);
+    else
+        ptx::tma_load_3d_pair(dst, map, bar, c0, c1, c2);
+}
+
+constexpr int kMnBoxBytes = 64 * kBK * 2;  // one MN-major box: 64 MN x 64 K elements
+
+template <typename T, int kCG, int kBN, int kAtoms, int kOp>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_sm100(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                        const __grid_constant__ CUtensorMap tmap_out,
                        const __grid_constant__ KernelParams p) {
     using C = TileCfg<kCG, kBN, kAtoms>;
-    // Tile N is a launch parameter (multiple of 32, at most kBN): the smem ring and TMEM are sized
-    // for kBN, a narrower tile uses the first bn/kCG weight rows of each atom and bn columns of
-    // each accumulator.
+    // A is MN-major for wgrad (dy^T), B is MN-major for both backward operations.
+    constexpr bool kAMn = kOp == kOpWgrad;
+    constexpr bool kBMn = kOp != kOpForward;
+    // Tile N is a launch parameter (multiple of 32, at most kBN; for an MN-major B also a multiple
+    // of 64 per CTA): the smem ring and TMEM are sized for kBN, a narrower tile uses the first
+    // bn/kCG B rows (columns) of each atom and bn columns of each accumulator.
     const int bn = p.bn;
     const int b_rows = bn / kCG;
-    const uint32_t idesc = ptx::f16_idesc(Fmt<T>::kUmma, kBM * kCG, bn);
+    const uint32_t idesc = ptx::f16_idesc(Fmt<T>::kUmma, kBM * kCG, bn, kAMn ? 1u : 0u, kBMn ? 1u : 0u);
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the 128-byte swizzle atoms.
@@ -246,8 +303,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::fence_proxy_async_smem();
     }
     if (warp == 0 && lane == 0) {
-        ptx::prefetch_tmap(&tmap_a);
-        ptx::prefetch_tmap(&tmap_b);
+        if constexpr (kOp != kOpWgrad) {  // wgrad loads through the per-group maps instead
+            ptx::prefetch_tmap(&tmap_a);
+            ptx::prefetch_tmap(&tmap_b);
+        }
         if (GG_TMA_STORE)
             ptx::prefetch_tmap(&tmap_out);
     }
@@ -265,6 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const Abort ab{p.status, abort_flag, p.timeout_ns};
     // Work units: every tile, or with split-K every (tile, K split). A split covers a contiguous
     // range of K atoms; each unit runs the same producer/MMA/epilogue pipeline over its range.
+    // (wgrad runs unsplit: its reduction length differs per group.)
     const int splits = p.splits > 1 ? p.splits : 1;
     const int total_units = p.total_tiles * splits;
     const int atoms_per_split = (p.num_kb + splits - 1) / splits;
@@ -277,14 +337,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
+            int fenced_g = -1;  // wgrad: group whose tensor maps this thread has acquired
             for (int u = cluster_id; u < total_units && ok; u += num_clusters) {
                 const int t = u / splits;
-                const int atom0 = (u - t * splits) * atoms_per_split;
-                const int atom1 = min(p.num_kb, atom0 + atoms_per_split);
+                const TileCoord tc = decode_tile<C::kClusterM, kOp>(p, t, cursor);
+                const int atom0 = kOp == kOpWgrad ? 0 : (u - t * splits) * atoms_per_split;
+                const int atom1 = kOp == kOpWgrad ? tc.red_atoms : min(p.num_kb, atom0 + atoms_per_split);
                 const int num_ks = (atom1 - atom0 + kAtoms - 1) / kAtoms;
-                const TileCoord tc = decode_tile<C::kClusterM>(p, t, cursor);
-                const int a_row = __ldg(&p.row_off[tc.g]) + tc.mt * C::kClusterM + int(cta_rank) * kBM;
+                // A: first row (forward/dgrad: token row; wgrad: row of dw[g], a column of dy)
+                const int a_row = (kOp == kOpWgrad ? 0 : tc.out_row0) + tc.mt * C::kClusterM + int(cta_rank) * kBM;
+                // B: first weight row (forward) / first output column (backward) of this CTA
                 const int b_row = tc.nt * bn + int(cta_rank) * b_rows;
+                const void *map_a = &tmap_a;
+                const void *map_b = &tmap_b;
+                if constexpr (kOp == kOpWgrad) {
+                    map_a = p.gmaps + 2 * tc.g;
+                    map_b = p.gmaps + 2 * tc.g + 1;
+                    if (tc.g != fenced_g && num_ks > 0) {
+                        ptx::fence_tensormap_acquire(map_a);
+                        ptx::fence_tensormap_acquire(map_b);
+                        fenced_g = tc.g;
+                    }
+                }
                 for (int ks = 0; ks < num_ks; ++ks) {
                     if (!wait_one(empty_bar(s), ph ^ 1u, ab, kStatusTimeout | kRoleProducer | uint32_t(s))) {
                         ok = false;
@@ -303,12 +377,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int a = 0; a < kAtoms; ++a) {
                         if (a < na && !skip) {
                             const int k0 = (atom0 + ks * kAtoms + a) * kBK;
-                            if constexpr (kCG == 1) {
-                                ptx::tma_load_2d(a_dst + a * C::kAAtomBytes, &tmap_a, fb, k0, a_row);
-                                ptx::tma_load_3d(b_dst + a * C::kBAtomBytes, &tmap_b, fb, k0, b_row, tc.g);
+                            const uint32_t ad = a_dst + a * C::kAAtomBytes;
+                            const uint32_t bd = b_dst + a * C::kBAtomBytes;
+                            if constexpr (kAMn) {
+                                // wgrad A = dy^T: two 64-column boxes of the group's dy rows
+                                load_2d<kCG>(ad, map_a, fb, a_row, k0);
+                                load_2d<kCG>(ad + kMnBoxBytes, map_a, fb, a_row + 64, k0);
                             } else {
-                                ptx::tma_load_2d_pair(a_dst + a * C::kAAtomBytes, &tmap_a, fb, k0, a_row);
-                                ptx::tma_load_3d_pair(b_dst + a * C::kBAtomBytes, &tmap_b, fb, k0, b_row, tc.g);
+                                load_2d<kCG>(ad, map_a, fb, k0, a_row);
+                            }
+                            if constexpr (kOp == kOpForward) {
+                                load_3d<kCG>(bd, map_b, fb, k0, b_row, tc.g);
+                            } else {
+                                for (int j = 0; j < b_rows / 64; ++j) {
+                                    if constexpr (kOp == kOpDgrad)  // w[g] rows k0.., columns b_row + 64j..
+                                        load_3d<kCG>(bd + j * kMnBoxBytes, map_b, fb, b_row + 64 * j, k0, tc.g);
+                                    else  // x rows (tokens) k0.. of the group, columns b_row + 64j..
+                                        load_2d<kCG>(bd + j * kMnBoxBytes, map_b, fb, b_row + 64 * j, k0);
+                                }
                             }
                         }
                     }
@@ -335,9 +421,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
+            int cursor = 0;
             for (int u = cluster_id; u < total_units && ok; u += num_clusters, ++tl) {
-                const int atom0 = (u - (u / splits) * splits) * atoms_per_split;
-                const int atom1 = min(p.num_kb, atom0 + atoms_per_split);
+                int atom0, atom1;
+                if constexpr (kOp == kOpWgrad) {
+                    atom0 = 0;
+                    atom1 = decode_tile<C::kClusterM, kOp>(p, u / splits, cursor).red_atoms;  // 0 for an empty group
+                } else {
+                    atom0 = (u - (u / splits) * splits) * atoms_per_split;
+                    atom1 = min(p.num_kb, atom0 + atoms_per_split);
+                }
                 const int num_ks = (atom1 - atom0 + kAtoms - 1) / kAtoms;
                 const int acc = int(tl & 1u);
                 const uint32_t acc_ph = (tl >> 1) & 1u;
@@ -357,16 +450,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ptx::tc_fence_after();
                     const int na = min(kAtoms, atom1 - (atom0 + ks * kAtoms));
                     const uint32_t a_addr = smem_base + uint32_t(s) * C::kStageBytes;
-                    const uint64_t adesc = ptx::sw128_kmajor_desc(a_addr);
-                    const uint64_t bdesc = ptx::sw128_kmajor_desc(a_addr + C::kABytes);
+                    const uint64_t adesc = kAMn ? ptx::sw128_mnmajor_desc(a_addr) : ptx::sw128_kmajor_desc(a_addr);
+                    const uint64_t bdesc = kBMn ? ptx::sw128_mnmajor_desc(a_addr + C::kABytes)
+                                                : ptx::sw128_kmajor_desc(a_addr + C::kABytes);
+                    // 16 K elements: 32 bytes along a K-major row, or 16 rows of 128 bytes MN-major
+                    constexpr int kStepA = kAMn ? 16 * 128 : 32;
+                    constexpr int kStepB = kBMn ? 16 * 128 : 32;
 #pragma unroll
                     for (int a = 0; a < kAtoms; ++a) {
                         if (a < na) {
 #pragma unroll
                             for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-                                // atom a, then 16 elements (32 bytes) along K inside the swizzle atom
-                                const uint64_t da = uint64_t((a * C::kAAtomBytes + kk * 32) >> 4);
-                                const uint64_t db = uint64_t((a * C::kBAtomBytes + kk * 32) >> 4);
+                                // atom a, then the kk-th 16-element K step inside the atom
+                                const uint64_t da = uint64_t((a * C::kAAtomBytes + kk * kStepA) >> 4);
+                                const uint64_t db = uint64_t((a * C::kBAtomBytes + kk * kStepB) >> 4);
                                 ptx::umma_f16<kCG>(d_tmem, adesc + da, bdesc + db, idesc,
                                                    (ks | a | kk) != 0 ? 1u : 0u);
                             }
@@ -406,14 +503,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int u = cluster_id; u < total_units; u += num_clusters, ++tl) {
             const int t = u / splits;
             const int split = u - t * splits;
-            const TileCoord tc = decode_tile<C::kClusterM>(p, t, cursor);
+            const TileCoord tc = decode_tile<C::kClusterM, kOp>(p, t, cursor);
             const int acc = int(tl & 1u);
             const uint32_t acc_ph = (tl >> 1) & 1u;
             if (!wait_warp(tfull_bar(acc), acc_ph, ab, kStatusTimeout | kRoleEpilogue | uint32_t(acc)))
                 break;
             ptx::tc_fence_after();
-            const int g_row0 = __ldg(&p.row_off[tc.g]);
-            const int m = __ldg(&p.row_off[tc.g + 1]) - g_row0;
+            const int g_row0 = tc.out_row0;
+            const int m = tc.rows;
+            // wgrad of an expert without tokens: no MMA ran, the tile is written as zeros
+            const bool zero_tile = kOp == kOpWgrad && tc.red_atoms == 0;
             const int local_row = tc.mt * C::kClusterM + int(cta_rank) * kBM + row_in_cta;
             const bool row_ok = local_row < m;
             const int64_t grow = int64_t(g_row0) + local_row;
@@ -468,6 +567,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t r[32];
                     ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + hh) * 32), r);
                     ptx::tmem_wait_ld(r);
+                    if (zero_tile) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            r[j] = 0u;
+                    }
 #pragma unroll
                     for (int jj = 0; jj < 4; ++jj) {
                         const int j = hh * 4 + jj;  // 16-byte chunk of the 128-byte row
@@ -490,6 +594,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t r[32];
                 ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
                 ptx::tmem_wait_ld(r);
+                if (zero_tile) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        r[j] = 0u;
+                }
                 const int col = tc.nt * bn + c * 32;
                 if (row_ok && splits > 1) {
                     // r = sum over splits 0..splits-1 in order; this unit's own part from TMEM

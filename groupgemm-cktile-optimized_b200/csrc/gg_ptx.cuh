@@ -100,6 +100,12 @@ __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
+// Before the first use of a tensor map that lives in global memory and was written through the
+// generic proxy (a host copy): order that write before the tensor-map proxy reads it.
+__device__ __forceinline__ void fence_tensormap_acquire(const void *tmap) {
+    asm volatile("fence.proxy.tensormap::generic.acquire.sys [%0], 128;" ::"l"(tmap) : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, uint32_t bar, int32_t c0,
                                             int32_t c1) {
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
@@ -246,11 +252,24 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
            (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
 
-// Instruction descriptor of tcgen05.mma kind::f16 with fp32 accumulation, both operands
-// K-major: bits 4-5 D format (1 = f32), 7-9 A format, 10-12 B format (0 = f16, 1 = bf16),
-// 15/16 A/B major (0 = K), 17-22 N >> 3, 24-28 M >> 4.
-__host__ __device__ constexpr uint32_t f16_idesc(uint32_t ab_fmt, int m, int n) {
-    return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (uint32_t(n >> 3) << 17) |
+// Shared-memory matrix descriptor for an MN-major operand tile written by TMA as boxes of 64
+// MN elements (one 128-byte row) x 64 K rows with the 128-byte swizzle: within a box the K rows
+// are 128 bytes apart in 8-row swizzle atoms of 1024 bytes; boxes of successive 64-element MN
+// chunks are 8 KB apart.
+//   leading-dimension byte offset = 8192 (between 64-element MN chunks)
+//   stride-dimension byte offset  = 1024 (between 8-row groups along K)
+// Sixteen K rows (one kind::f16 MMA) span 2048 bytes.
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t saddr) {
+    return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t(8192 >> 4) << 16) | (uint64_t(1024 >> 4) << 32) |
+           (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16 with fp32 accumulation: bits 4-5 D format
+// (1 = f32), 7-9 A format, 10-12 B format (0 = f16, 1 = bf16), 15/16 A/B major (0 = K-major,
+// 1 = MN-major), 17-22 N >> 3, 24-28 M >> 4.
+__host__ __device__ constexpr uint32_t f16_idesc(uint32_t ab_fmt, int m, int n, uint32_t a_mn = 0,
+                                                 uint32_t b_mn = 0) {
+    return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (a_mn << 15) | (b_mn << 16) | (uint32_t(n >> 3) << 17) |
            (uint32_t(m >> 4) << 24);
 }
 

@@ -75,6 +75,40 @@ const char *gg_name(const gg_handle *h);
  * and why_len > 0) when the shape is refused, or a negative error. */
 int gg_prepare(gg_handle *h, const gg_problem *p, gg_stream_t stream, char *why, size_t why_len);
 
+/* Backward grouped GEMMs of the same layer (MoE training). The reference benchmarks the forward
+ * op only; its vendored Primus-Turbo grouped GEMM carries the two backward calls this replaces
+ * (third_party/primus_turbo/kernels/hipblaslt_grouped_gemm.cu:80-96 shape rules,
+ * :199-240 per-group arguments, zero-filled gradient for an expert without tokens :201-214):
+ *
+ *   GG_OP_DGRAD: dx[rows of g] = dy[rows of g] @ w[g]     dx [sum(group_m), k]
+ *   GG_OP_WGRAD: dw[g] = dy[rows of g]^T @ x[rows of g]   dw [group_num, n, k]; an expert with
+ *                                                         group_m[g] == 0 gets dw[g] = 0
+ *
+ * with dy [sum(group_m), n] (the gradient of out), x and w as in gg_problem. Same dtype rules,
+ * fp32 accumulation, output in the input dtype (dw is overwritten, not accumulated into). */
+enum gg_op { GG_OP_FORWARD = 0, GG_OP_DGRAD = 1, GG_OP_WGRAD = 2 };
+
+typedef struct gg_grad_problem {
+    int32_t dtype;          /* enum gg_dtype */
+    int32_t group_num;      /* B */
+    int64_t n;              /* N: columns of dy = rows of each w[g] */
+    int64_t k;              /* K: columns of x, dx and each w[g] */
+    const int64_t *group_m; /* host, [group_num] tokens per group */
+    const void *dy;         /* device, [sum(group_m), n] */
+    const void *x;          /* device, [sum(group_m), k]  (GG_OP_WGRAD) */
+    const void *w;          /* device, [group_num, n, k]  (GG_OP_DGRAD) */
+    void *dx;               /* device, [sum(group_m), k]  (GG_OP_DGRAD output) */
+    void *dw;               /* device, [group_num, n, k]  (GG_OP_WGRAD output) */
+} gg_grad_problem;
+
+/* Backend::prepare() for a backward operation `op` (GG_OP_DGRAD or GG_OP_WGRAD); afterwards
+ * gg_run() enqueues it as one kernel launch and gg_detail() describes it. The operands the
+ * operation does not use may be NULL. Extra refusals: "split" > 1 for wgrad (its reduction
+ * length differs per group), group_num * n >= 2^31 for wgrad, and a forced "bn" that is not a
+ * multiple of 64 per CTA (the MN-major operand boxes are 64 columns wide). */
+int gg_prepare_grad(gg_handle *h, const gg_grad_problem *p, int32_t op, gg_stream_t stream, char *why,
+                    size_t why_len);
+
 /* Backend::run() (common/backend.hpp:67; ck_kernel/ck_grouped_gemm.cpp:140, :114-121). Timed:
  * enqueues exactly one kernel launch on `stream` and does not synchronise. */
 int gg_run(gg_handle *h, gg_stream_t stream);

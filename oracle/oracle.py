@@ -148,3 +148,49 @@ def check16(got_bits: np.ndarray, ref: np.ndarray, dtype: int):
     first = ctypes.c_int64(-1)
     bad = lib().orc_check16(_ptr(got_bits), _ptr(ref), got_bits.size, dtype, ctypes.byref(mx), ctypes.byref(first))
     return int(bad), float(mx.value), int(first.value)
+
+
+# ---- backward grouped GEMMs ---------------------------------------------------------------
+# The reference benchmarks the forward op only. Its vendored Primus-Turbo grouped GEMM defines
+# the two backward calls of the same MoE layer (third_party/primus_turbo/kernels/
+# hipblaslt_grouped_gemm.cu:80-96 shape rules, :199-240 per-group arguments): grad_a = grad_c x b
+# (non-transA) and grad_b = a^T x grad_c (transA), with an expert that received no tokens given a
+# zero gradient (:201-214). These restate that math in float64 on the decoded 16-bit inputs and
+# return float32, the precision the forward oracle's pass rule compares against.
+
+def make_grad_inputs(group_m, n: int, k: int, dtype: int, threads: int = 0):
+    """dy [sum(M), n] (seed 3) plus x (seed 1) and w (seed 2) as in make_inputs, as 16-bit patterns.
+    The reference has no backward harness; seed 3 continues its seed numbering."""
+    x, w = make_inputs(group_m, n, k, dtype, threads)
+    dy = fill_randn(int(sum(group_m)) * n, 3, dtype, threads).reshape(int(sum(group_m)), n)
+    return dy, x, w
+
+
+def grouped_dgrad_f32(dy: np.ndarray, w: np.ndarray, group_m, dtype: int) -> np.ndarray:
+    """dx [sum(M), k] = dy[rows of g] @ w[g] (hipblaslt_grouped_gemm.cu:91-95, non-transA)."""
+    G, n, k = w.shape
+    dyf = to_f32(dy, dtype).astype(np.float64).reshape(-1, n)
+    wf = to_f32(w, dtype).astype(np.float64)
+    out = np.zeros((dyf.shape[0], k), np.float32)
+    r0 = 0
+    for g, m in enumerate(group_m):
+        if m:
+            out[r0:r0 + m] = dyf[r0:r0 + m] @ wf[g]
+        r0 += int(m)
+    return out
+
+
+def grouped_wgrad_f32(dy: np.ndarray, x: np.ndarray, group_m, dtype: int) -> np.ndarray:
+    """dw [G, n, k], dw[g] = dy[rows of g]^T @ x[rows of g]; zero for an empty group
+    (hipblaslt_grouped_gemm.cu:82-90 transA, :201-214)."""
+    n = dy.shape[-1]
+    k = x.shape[-1]
+    dyf = to_f32(dy, dtype).astype(np.float64).reshape(-1, n)
+    xf = to_f32(x, dtype).astype(np.float64).reshape(-1, k)
+    out = np.zeros((len(group_m), n, k), np.float32)
+    r0 = 0
+    for g, m in enumerate(group_m):
+        if m:
+            out[g] = dyf[r0:r0 + m].T @ xf[r0:r0 + m]
+        r0 += int(m)
+    return out

@@ -116,3 +116,41 @@ def test_null_handle_is_rejected(gg):
     assert lib.gg_device_status(None, None, ctypes.byref(st)) == gg.GG_ERR_ARG
     lib.gg_release(None)
     lib.gg_destroy(None)
+
+
+@pytest.mark.parametrize(
+    "op,kw,reason",
+    [
+        ("dgrad", dict(dtype=3), "dtype"),
+        ("dgrad", dict(k=100), "k must be a multiple of 8"),
+        ("dgrad", dict(w=0), "dy, w and dx must be non-null"),
+        ("dgrad", dict(dx=ALIGNED + 4), "16-byte aligned"),
+        ("wgrad", dict(x=0), "dy, x and dw must be non-null"),
+        ("wgrad", dict(group_m=[0, 0], dw=0), "dy, x and dw must be non-null"),
+        ("wgrad", dict(group_m=[4, -2]), "group_m"),
+        ("wgrad", dict(group_num_n=True), "group_num * n"),
+    ],
+)
+def test_prepare_grad_refuses_unsupported_arguments(gg, op, kw, reason):
+    args = dict(dtype=gg.BF16, group_m=[4, 4], n=64, k=64, dy=ALIGNED, x=ALIGNED, w=ALIGNED, dx=ALIGNED,
+                dw=ALIGNED)
+    if kw.pop("group_num_n", False):
+        args.update(group_m=[1] * 64, n=1 << 26)
+    args.update(kw)
+    b = gg.B200Backend()
+    why = b.prepare_grad(gg.OP_DGRAD if op == "dgrad" else gg.OP_WGRAD, args["dtype"], args["group_m"], args["n"],
+                         args["k"], dy_ptr=args["dy"], x_ptr=args["x"], w_ptr=args["w"], dx_ptr=args["dx"],
+                         dw_ptr=args["dw"])
+    assert reason in why, why
+    with pytest.raises(gg.GGError):
+        b.run()
+
+
+def test_prepare_grad_rejects_unknown_op_and_wgrad_split(gg):
+    b = gg.B200Backend()
+    with pytest.raises(gg.GGError) as e:
+        b.prepare_grad(7, gg.BF16, [4], 64, 64, dy_ptr=ALIGNED, x_ptr=ALIGNED, dw_ptr=ALIGNED)
+    assert e.value.code == gg.GG_ERR_ARG
+    b.set_option("split", 2)
+    assert "wgrad" in b.prepare_grad(gg.OP_WGRAD, gg.BF16, [4], 64, 64, dy_ptr=ALIGNED, x_ptr=ALIGNED,
+                                     dw_ptr=ALIGNED)

@@ -178,3 +178,34 @@ def test_check_rule(orc):
     nan[0] = np.nan
     bad, mx = orc.check(nan, ref)
     assert bad == 1 and mx == np.inf
+
+
+@pytest.mark.parametrize("dt", [0, 1])
+def test_backward_oracle_matches_forward_oracle_on_transposed_operands(orc, dt):
+    # dgrad: dx = dy @ w[g] is the forward op with weights w[g]^T ([G, k, n]).
+    # wgrad: dw[g] = dy_g^T @ x_g is the forward op of one group with x' = dy_g^T, w' = x_g^T.
+    group_m = [5, 0, 70, 33]
+    n, k = 48, 40
+    dy, x, w = orc.make_grad_inputs(group_m, n, k, dt)
+    dx = orc.grouped_dgrad_f32(dy, w, group_m, dt)
+    wt = np.ascontiguousarray(np.transpose(w, (0, 2, 1)))
+    assert np.allclose(dx, orc.grouped_gemm_f32(dy, wt, group_m, dt), rtol=1e-5, atol=1e-4)
+    dw = orc.grouped_wgrad_f32(dy, x, group_m, dt)
+    assert dw.shape == (4, n, k)
+    r0 = 0
+    for g, m in enumerate(group_m):
+        if m == 0:
+            assert np.all(dw[g] == 0)
+        else:
+            xt = np.ascontiguousarray(dy[r0:r0 + m].T)
+            wg = np.ascontiguousarray(x[r0:r0 + m].T)[None]
+            assert np.allclose(dw[g], orc.grouped_gemm_f32(xt, wg, [n], dt), rtol=1e-5, atol=1e-4)
+        r0 += m
+
+
+def test_grad_inputs_are_deterministic(orc):
+    a = orc.make_grad_inputs([3, 4], 16, 8, 0)
+    b = orc.make_grad_inputs([3, 4], 16, 8, 0)
+    for u, v in zip(a, b):
+        assert np.array_equal(u, v)
+    assert a[0].shape == (7, 16) and a[1].shape == (7, 8) and a[2].shape == (2, 16, 8)
