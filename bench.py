@@ -246,6 +246,108 @@ def load_traffic(cfg_name):
         return None
 
 
+def run_backward(args, cfg):
+    """Device-timed backward grouped GEMM (dgrad or wgrad) on one GPU, beside a per-group cuBLAS
+    loop (torch.matmul) of the same op on the same tensors. One JSON line; not the driver's
+    headline (that is the forward op)."""
+    import torch
+
+    gg = load_package()
+    op = gg.OP_DGRAD if args.op == "dgrad" else gg.OP_WGRAD
+    dtype = gg.DTYPES[cfg["dtype"]]
+    tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
+    torch.cuda.set_device(0)
+    total_groups, (g0, g1) = shard_of(cfg, 1, 0, gg)
+    ng = g1 - g0
+    n, k = cfg["n"], cfg["k"]
+    group_m = group_sizes(cfg, g0, g1)
+    rows = sum(group_m)
+    gen = torch.Generator(device="cuda").manual_seed(1000)
+    dy = torch.randn(rows, n, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
+    if op == gg.OP_DGRAD:
+        b_op = torch.empty(ng, n, k, device="cuda", dtype=tdt)
+        for g in range(ng):
+            b_op[g] = torch.randn(n, k, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
+        out = torch.empty(rows, k, device="cuda", dtype=tdt)
+    else:
+        b_op = torch.randn(rows, k, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
+        out = torch.empty(ng, n, k, device="cuda", dtype=tdt)
+    stream = torch.cuda.Stream()
+    s = stream.cuda_stream
+    be = gg.make_b200_backend()
+    if args.variant >= 0:
+        be.set_option("variant", args.variant)
+    if op == gg.OP_DGRAD:
+        why = be.prepare_grad(op, dtype, group_m, n, k, dy_ptr=dy.data_ptr(), w_ptr=b_op.data_ptr(),
+                              dx_ptr=out.data_ptr(), stream=s)
+    else:
+        why = be.prepare_grad(op, dtype, group_m, n, k, dy_ptr=dy.data_ptr(), x_ptr=b_op.data_ptr(),
+                              dw_ptr=out.data_ptr(), stream=s)
+    if why:
+        raise SystemExit(f"prepare_grad refused the workload: {why}")
+    offs = np.concatenate([[0], np.cumsum(group_m)]).tolist()
+
+    def cublas_step(dst):
+        for g in range(ng):
+            a, b = offs[g], offs[g + 1]
+            if op == gg.OP_DGRAD:
+                torch.matmul(dy[a:b], b_op[g], out=dst[a:b])
+            else:
+                torch.matmul(dy[a:b].t(), b_op[a:b], out=dst[g])
+
+    def timed(fn, steps):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize()
+            ev0.record(stream)
+            for _ in range(steps):
+                fn()
+            ev1.record(stream)
+        ev1.synchronize()
+        return ev0.elapsed_time(ev1) / steps
+
+    with ClockSampler(0) as clocks:
+        ms = timed(lambda: be.run(s), args.steps)
+    if be.device_status(s) != 0:
+        raise SystemExit("kernel reported a bounded-wait timeout")
+    ref = torch.empty_like(out)
+    ms_cublas = timed(lambda: cublas_step(ref), max(3, args.steps // 5))
+    # spot check against cuBLAS on the same tensors: the reference pass rule on every element
+    with torch.cuda.stream(stream):
+        be.run(s)
+        cublas_step(ref)
+    torch.cuda.synchronize()
+    lim = min(out.numel(), 1 << 26)  # the first 64M elements (bounded temporaries)
+    o32, r32 = out.view(-1)[:lim].float(), ref.view(-1)[:lim].float()
+    diff = (o32 - r32).abs()
+    bad = int((diff > 1e-2 + 2e-2 * r32.abs()).sum().item())
+    flops = 2.0 * rows * n * k
+    value = flops / (ms * 1e-3) / 1e12
+    peaks, peak_src = measured_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK["bf16_tflops"]))
+    line = {
+        "metric": f"grouped-GEMM TFLOPS/GPU ({cfg['dtype']}), backward {args.op}", "op": args.op,
+        "value": round(value, 2), "unit": "TFLOPS", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": cfg["dtype"],
+        "data": "synthetic N(0,1) (torch generator on the device)",
+        "config": {"workload": cfg["desc"], "op": ("dx = dy @ w[g]" if op == gg.OP_DGRAD
+                                                   else "dw[g] = dy[g]^T @ x[g]"),
+                   "l2": "inputs larger than L2 (no flush)" if rows * (n + k) * 2 > 126e6 else "inputs may fit in L2"},
+        "roofline": {"bound": "tensor", "achieved": round(value, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(value / peak, 4), "peak_source": f"{peak_src} bf16 burst (cuBLAS)"},
+        "cublas_loop": {"value": round(flops / (ms_cublas * 1e-3) / 1e12, 2), "unit": "TFLOPS",
+                        "ms_per_step": round(ms_cublas, 4), "how": "torch.matmul per expert, one stream"},
+        "check_vs_cublas": {"elements": int(lim), "outside_tolerance": bad,
+                            "max_abs_diff": float(diff.max().item())},
+        "gpu_launches": args.steps, "clocks": clocks.summary(), "detail": be.detail(),
+    }
+    be.release()
+    print(json.dumps(line), flush=True)
+    return 0 if bad == 0 else 1
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -257,10 +359,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--allgather", action="store_true", help="also time an NCCL all-gather of the outputs")
     ap.add_argument("--variant", type=int, default=-1)
+    ap.add_argument("--op", default="forward", choices=["forward", "dgrad", "wgrad"],
+                    help="dgrad/wgrad: time a backward grouped GEMM on one GPU (not the headline line)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     if args.warmup < 3:
         args.warmup = 3  # timing rule: at least 3 warm-up steps
+    if args.op != "forward" and args.impl == "ours":
+        return run_backward(args, cfg)
 
     if args.impl == "reference":
         return run_reference(args, cfg)

@@ -108,6 +108,18 @@ public:
         throw CudaError(gg_last_error(h_));
     }
 
+    // Backward grouped GEMM of the same layer (GG_OP_DGRAD or GG_OP_WGRAD, gg_prepare_grad);
+    // run()/release()/detail() then apply to it. Returns "" or the N/A reason.
+    std::string prepare_grad(const gg_grad_problem &q, int32_t op, cudaStream_t stream) {
+        char why[256];
+        const int rc = gg_prepare_grad(h_, &q, op, stream, why, sizeof(why));
+        if (rc == GG_OK)
+            return "";
+        if (rc == GG_NOT_SUPPORTED)
+            return why;
+        throw CudaError(gg_last_error(h_));
+    }
+
     void run(cudaStream_t stream) override {
         if (gg_run(h_, stream) != GG_OK)
             throw CudaError(gg_last_error(h_));
