@@ -87,11 +87,13 @@ struct gg_handle {
     // options
     int opt_variant = -1;
     int opt_band = 0;
+    int opt_raster = -1;
     int opt_bn = 0;
     int opt_split = 0;
     int opt_max_ctas = 0;
     int64_t opt_timeout_ms = 2000;
     int opt_test_stall = 0;
+    int opt_pdl = 1;
 
     // prepared state
     bool ready = false;
@@ -252,6 +254,10 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < 0 || value > 1024)
             return fail(h, GG_ERR_ARG, "band must be 0..1024");
         h->opt_band = int(value);
+    } else if (!std::strcmp(key, "raster")) {
+        if (value < -1 || value > 1)
+            return fail(h, GG_ERR_ARG, "raster must be -1 (auto), 0 (m-tile bands) or 1 (n-tile bands)");
+        h->opt_raster = int(value);
     } else if (!std::strcmp(key, "split")) {
         if (value < 0 || value > 8)
             return fail(h, GG_ERR_ARG, "split must be 0 (auto) or 1..8");
@@ -268,6 +274,10 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < 1 || value > 60000)
             return fail(h, GG_ERR_ARG, "timeout_ms must be 1..60000");
         h->opt_timeout_ms = value;
+    } else if (!std::strcmp(key, "pdl")) {
+        if (value != 0 && value != 1)
+            return fail(h, GG_ERR_ARG, "pdl must be 0 or 1");
+        h->opt_pdl = int(value);
     } else if (!std::strcmp(key, "test_stall")) {
         if (value != 0 && value != 1)
             return fail(h, GG_ERR_ARG, "test_stall must be 0 or 1");
@@ -513,7 +523,8 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
         GG_CUDA(h, cudaMalloc(&h->d_status, 16));
     GG_CUDA(h, cudaMemsetAsync(h->d_status, 0, 16, stream));
     if (ch.splits > 1) {
-        const size_t ws_bytes = size_t(ch.splits) * size_t(total_m) * size_t(out_cols) * sizeof(float);
+        // tile-private partials: per tile and CTA, 128 rows x bn fp32 per split
+        const size_t ws_bytes = size_t(tiles) * size_t(v.cg) * size_t(ch.splits) * 128 * size_t(bn) * sizeof(float);
         const size_t ctr_bytes = size_t(tiles) * size_t(v.cg) * 4 * sizeof(int32_t);
         if (h->ws_cap < ws_bytes) {
             if (h->d_ws)
@@ -592,6 +603,7 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
 
     // ---- raster band and persistent grid ----
     int band = h->opt_band;
+    const int raster = h->opt_raster < 0 ? 0 : h->opt_raster;
     if (band <= 0) {
         // Enough m-tiles per band that one wave of tiles spans few weight panels.
         band = v.cg == 2 ? 8 : 16;
@@ -621,8 +633,8 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     kp.splits = ch.splits;
     kp.ws = ch.splits > 1 ? h->d_ws : nullptr;
     kp.counters = ch.splits > 1 ? h->d_counters : nullptr;
-    kp.ws_stride = total_m * out_cols;
     kp.band = band;
+    kp.raster = raster;
     kp.test_stall = h->opt_test_stall;
     kp.timeout_ns = uint64_t(h->opt_timeout_ms) * 1000000ull;
 
@@ -638,9 +650,10 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     h->cg = v.cg;
     char d[256];
     std::snprintf(d, sizeof(d),
-                  "gg_sm100<%s%s%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld split=%d grid=%d band=%d",
+                  "gg_sm100<%s%s%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld split=%d grid=%d band=%d%s",
                   q.dtype == GG_BF16 ? "bf16" : "fp16", op == gg::kOpForward ? "" : ",", op == gg::kOpForward ? "" : op_name(op),
-                  v.cluster_m, bn, gg::kBK * v.atoms, v.cg, v.stages, (long long)tiles, ch.splits, h->grid, band);
+                  v.cluster_m, bn, gg::kBK * v.atoms, v.cg, v.stages, (long long)tiles, ch.splits, h->grid, band,
+                  raster ? "n" : "");
     h->detail = d;
     h->ready = true;
     return GG_OK;
@@ -692,17 +705,22 @@ int gg_run(gg_handle *h, gg_stream_t stream) {
     if (h->params.total_tiles == 0)
         return GG_OK;  // every group empty: nothing to write
     cudaLaunchConfig_t cfg{};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = unsigned(h->cg);
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // Programmatic dependent launch: this grid may be scheduled while the previous kernel in the
+    // stream finishes; the kernel waits for it (griddepcontrol.wait) before reading or writing
+    // global memory, so only launch latency and on-chip set-up overlap.
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(unsigned(h->grid), 1, 1);
     cfg.blockDim = dim3(gg::kThreads, 1, 1);
     cfg.dynamicSmemBytes = size_t(h->smem);
     cfg.stream = stream;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = h->opt_pdl ? 2 : 1;
     void *args[4] = {&h->tmap_a, &h->tmap_b, &h->tmap_out, &h->params};
     GG_CUDA(h, cudaLaunchKernelExC(&cfg, h->fn, args));
     return GG_OK;

@@ -94,10 +94,10 @@ struct KernelParams {
     int32_t bn;           // tile N of this launch: a multiple of 32, <= the variant's kBN
     int32_t total_tiles;  // tile_off[G]
     int32_t splits;       // K splits per tile (0 or 1 = none); work units = total_tiles x splits
-    float *ws;            // splits > 1: fp32 partial sums, [splits][sum(M)][N]
+    float *ws;            // splits > 1: fp32 partial sums, per tile [kCG][4 warps][splits][bn/32] 4-KB blocks
     int32_t *counters;    // splits > 1: [total_tiles][kCG][4] arrival counts, 0 between launches
-    int64_t ws_stride;    // sum(M) * N
-    int32_t band;         // M tiles per raster band (L2 reuse of the weight panel)
+    int32_t band;         // tiles per raster band (L2 reuse, see decode_tile)
+    int32_t raster;       // 0: bands of `band` m-tiles, n-tiles swept; 1: bands of `band` n-tiles
     int32_t test_stall;   // test only: 1 = the first stage of cluster 0 is never loaded, so the
                           // MMA wait on it runs out and the status word reports it
     uint64_t timeout_ns;
@@ -148,10 +148,14 @@ struct TileCoord {
 };
 
 // Map a linear tile index to (group, m-tile, n-tile). Within a group, tiles are rastered in
-// bands of `band` m-tiles: all n-tiles of a band are visited m-fastest, so concurrently
-// running tiles share one weight panel (n-tile) and the band's activation rows stay in L2 —
-// the role CK's GemmSpatiallyLocalTilePartitioner<8,4> plays in the reference
-// (ck_kernel/ck_grouped_gemm_config.hpp:74-77).
+// bands (the role CK's GemmSpatiallyLocalTilePartitioner<8,4> plays in the reference,
+// ck_kernel/ck_grouped_gemm_config.hpp:74-77):
+//   raster 0: bands of `band` m-tiles; all n-tiles of a band are visited m-fastest, so
+//             concurrently running tiles share a weight panel and the band's activation rows
+//             stay in L2 (each weight panel is read from DRAM once per band);
+//   raster 1: bands of `band` n-tiles; all m-tiles of a band are visited n-fastest, so the band's
+//             weight panels stay in L2 and each activation row block is read from DRAM once per
+//             band (with one band covering every n-tile: each operand once).
 template <int kClusterM, int kOp>
 __device__ __forceinline__ TileCoord decode_tile(const KernelParams &p, int t, int &cursor) {
     while (__ldg(&p.tile_off[cursor + 1]) <= t)
@@ -171,12 +175,21 @@ __device__ __forceinline__ TileCoord decode_tile(const KernelParams &p, int t, i
         tc.red_atoms = p.num_kb;
     }
     const int tiles_m = (tc.rows + kClusterM - 1) / kClusterM;
-    const int band_tiles = p.band * p.tiles_n;
-    const int b = local / band_tiles;
-    const int r = local - b * band_tiles;
-    const int rows = min(p.band, tiles_m - b * p.band);
-    tc.nt = r / rows;
-    tc.mt = b * p.band + (r - tc.nt * rows);
+    if (p.raster == 0) {
+        const int band_tiles = p.band * p.tiles_n;
+        const int b = local / band_tiles;
+        const int r = local - b * band_tiles;
+        const int rows = min(p.band, tiles_m - b * p.band);
+        tc.nt = r / rows;
+        tc.mt = b * p.band + (r - tc.nt * rows);
+    } else {
+        const int band_tiles = p.band * tiles_m;
+        const int b = local / band_tiles;
+        const int r = local - b * band_tiles;
+        const int cols = min(p.band, p.tiles_n - b * p.band);
+        tc.mt = r / cols;
+        tc.nt = b * p.band + (r - tc.mt * cols);
+    }
     return tc;
 }
 
@@ -320,6 +333,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::cluster_sync();  // peer barriers are initialised before any remote arrive
     ptx::tc_fence_after();
     const uint32_t tmem_base = *tmem_ptr_slot;
+    // Everything above is on-chip set-up. With programmatic dependent launch it overlaps the
+    // previous kernel's tail; global memory is touched only after this wait.
+    ptx::griddep_wait();
+    ptx::griddep_launch_dependents();
 
     const Abort ab{p.status, abort_flag, p.timeout_ns};
     // Work units: every tile, or with split-K every (tile, K split). A split covers a contiguous
@@ -327,7 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // (wgrad runs unsplit: its reduction length differs per group.)
     const int splits = p.splits > 1 ? p.splits : 1;
     const int total_units = p.total_tiles * splits;
-    const int atoms_per_split = (p.num_kb + splits - 1) / splits;
+    // Split i covers K atoms [i * num_kb / splits, (i + 1) * num_kb / splits): balanced, and never
+    // empty while splits <= num_kb (the host refuses more splits than atoms).
 
     if (warp == 0) {
         // ---------------- TMA producer (one thread) ----------------
@@ -341,8 +359,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int u = cluster_id; u < total_units && ok; u += num_clusters) {
                 const int t = u / splits;
                 const TileCoord tc = decode_tile<C::kClusterM, kOp>(p, t, cursor);
-                const int atom0 = kOp == kOpWgrad ? 0 : (u - t * splits) * atoms_per_split;
-                const int atom1 = kOp == kOpWgrad ? tc.red_atoms : min(p.num_kb, atom0 + atoms_per_split);
+                const int atom0 = kOp == kOpWgrad ? 0 : (u - t * splits) * p.num_kb / splits;
+                const int atom1 = kOp == kOpWgrad ? tc.red_atoms : (u - t * splits + 1) * p.num_kb / splits;
                 const int num_ks = (atom1 - atom0 + kAtoms - 1) / kAtoms;
                 // A: first row (forward/dgrad: token row; wgrad: row of dw[g], a column of dy)
                 const int a_row = (kOp == kOpWgrad ? 0 : tc.out_row0) + tc.mt * C::kClusterM + int(cta_rank) * kBM;
@@ -428,8 +446,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     atom0 = 0;
                     atom1 = decode_tile<C::kClusterM, kOp>(p, u / splits, cursor).red_atoms;  // 0 for an empty group
                 } else {
-                    atom0 = (u - (u / splits) * splits) * atoms_per_split;
-                    atom1 = min(p.num_kb, atom0 + atoms_per_split);
+                    const int sp = u - (u / splits) * splits;
+                    atom0 = sp * p.num_kb / splits;
+                    atom1 = (sp + 1) * p.num_kb / splits;
                 }
                 const int num_ks = (atom1 - atom0 + kAtoms - 1) / kAtoms;
                 const int acc = int(tl & 1u);
@@ -519,24 +538,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             T *orow = out + grow * p.n;
             const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * kBN);
             bool store_out = true;
+            const int nch = bn / 32;  // 32-column chunks of the tile
+            // split-K: first float4 of this warp's workspace region (splits x nch blocks of 4 KB)
+            const int64_t ws_warp = ((int64_t(t) * kCG + int(cta_rank)) * 4 + q) * int64_t(splits) * nch * 256;
             if (splits > 1) {
                 // Split-K: publish this unit's fp32 partial; the last of the tile's splits to
                 // arrive (per CTA and warp) sums all of them in split order and stores out.
-                float *wrow = p.ws + int64_t(split) * p.ws_stride + grow * p.n;
+                // This warp's workspace blocks of the tile: [split][chunk], each block the 32 x 32
+                // fp32 fragment of one tcgen05.ld in lane order (float4 j of lane l at j * 32 + l),
+                // so every warp access is 512 contiguous bytes.
+                float4 *wsw = reinterpret_cast<float4 *>(p.ws) + ws_warp + (int64_t(split) * nch) * 256 + lane;
 #pragma unroll 1
-                for (int c = 0; c < bn / 32; ++c) {
+                for (int c = 0; c < nch; ++c) {
                     uint32_t r[32];
                     ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
                     ptx::tmem_wait_ld(r);
-                    const int col = tc.nt * bn + c * 32;
-                    if (row_ok) {
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            if (col + j * 4 < p.n)
-                                __stcg(reinterpret_cast<float4 *>(wrow + col + j * 4),
-                                       make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
-                    }
+                    for (int j = 0; j < 8; ++j)
+                        __stcg(wsw + c * 256 + j * 32,
+                               make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                           __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
                 }
                 __threadfence();
                 __syncwarp();
@@ -589,6 +610,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 out_buf ^= 1;
             }
+            // Split-K reduction by the last arriver: the other splits' blocks are read in (chunk,
+            // split) order with one block always in flight ahead of the one being added.
+            const int others = splits - 1;
+            auto other_blk = [&](int idx) {
+                const int c = idx / others;
+                const int o = idx - c * others;
+                const int s2 = o + (o >= split ? 1 : 0);
+                return reinterpret_cast<const float4 *>(p.ws) + ws_warp + (int64_t(s2) * nch + c) * 256 + lane;
+            };
+            float4 nxt[8];
+            int blk = 0;
+            if (store_out && splits > 1) {
+                const float4 *src = other_blk(0);
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    nxt[j] = __ldcg(src + j * 32);
+            }
 #pragma unroll 1
             for (int c = c_tma; store_out && c < bn / 32; ++c) {
                 uint32_t r[32];
@@ -600,8 +638,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         r[j] = 0u;
                 }
                 const int col = tc.nt * bn + c * 32;
-                if (row_ok && splits > 1) {
-                    // r = sum over splits 0..splits-1 in order; this unit's own part from TMEM
+                if (splits > 1) {
+                    // r = sum over splits 0..splits-1 in that order; this unit's own part from TMEM
                     float sum[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
@@ -612,16 +650,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                             for (int j = 0; j < 32; ++j)
                                 sum[j] += __uint_as_float(r[j]);
                         } else {
-                            const float *prow = p.ws + int64_t(s2) * p.ws_stride + grow * p.n + col;
+                            float4 cur[8];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                cur[j] = nxt[j];
+                            if (++blk < nch * others) {
+                                const float4 *src = other_blk(blk);
+#pragma unroll
+                                for (int j = 0; j < 8; ++j)
+                                    nxt[j] = __ldcg(src + j * 32);
+                            }
 #pragma unroll
                             for (int j = 0; j < 8; ++j) {
-                                if (col + j * 4 < p.n) {
-                                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(prow + j * 4));
-                                    sum[4 * j] += v.x;
-                                    sum[4 * j + 1] += v.y;
-                                    sum[4 * j + 2] += v.z;
-                                    sum[4 * j + 3] += v.w;
-                                }
+                                sum[4 * j] += cur[j].x;
+                                sum[4 * j + 1] += cur[j].y;
+                                sum[4 * j + 2] += cur[j].z;
+                                sum[4 * j + 3] += cur[j].w;
                             }
                         }
                     }

@@ -42,6 +42,17 @@ __device__ __forceinline__ void cluster_sync() {
                  "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// ---- programmatic dependent launch ----
+// Wait until the grids this one depends on (the previous kernel in the stream, when launched
+// with programmatic stream serialisation) have completed and their memory is visible. Returns
+// at once when there is none.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next grid in the stream (if launched with programmatic stream serialisation) to be
+// scheduled; it still waits in its own griddep_wait() for this grid to complete.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- mbarrier ----
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");

@@ -301,3 +301,27 @@ def test_config_expert_parallel_shards_equal_whole(gg, orc):
         bs.run(s)
         assert bs.device_status(s) == 0
         assert torch.equal(shard.view(torch.int16), out[g0 * M:g1 * M].view(torch.int16)), f"shard {r}"
+
+
+@pytest.mark.parametrize("variant,split", [(0, 4), (0, 6), (1, 5), (2, 6)])
+def test_split_k_more_splits_than_atom_pairs(gg, orc, variant, split):
+    """K = 384 is 6 atoms of 64: splits up to 6 must each get a non-empty K range (a ceiling
+    partition would leave the last split with none)."""
+    torch = _torch()
+    group_m, n, k = [256, 100], 512, 384
+    x, w = orc.make_inputs(group_m, n, k, 0)
+    ref = orc.grouped_gemm_f32(x, w, group_m, 0)
+    xd, wd = upload(torch, x), upload(torch, w)
+    out = torch.full((sum(group_m) * n + GUARD,), CANARY, dtype=torch.int16, device="cuda")
+    b = gg.B200Backend()
+    b.set_option("variant", variant)
+    b.set_option("split", split)
+    s = torch.cuda.current_stream().cuda_stream
+    assert b.prepare(0, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s) == ""
+    assert f"split={split}" in b.detail(), b.detail()
+    b.run(s)
+    assert b.device_status(s) == 0
+    res = out.cpu().numpy().view(np.uint16)
+    assert np.all(res[sum(group_m) * n:] == CANARY)
+    bad, mx, first = orc.check16(res[: sum(group_m) * n].reshape(-1, n), ref, 0)
+    assert bad == 0, (b.detail(), bad, mx, first)
