@@ -47,6 +47,8 @@ CONFIGS = {
               desc="D: B=32 experts per GPU, M=2048, N=7168, K=2048, fp16 (BASELINE configs[2])"),
     "P": dict(b=16, m=1000, n=2880, k=2880, dtype="bf16", per_gpu=True,
               desc="P: B=16 experts per GPU, M=1000, N=2880, K=2880, bf16 (BASELINE configs[3])"),
+    "P1": dict(b=1, m=1000, n=2880, k=2880, dtype="bf16", per_gpu=True,
+               desc="P1: B=1 expert, M=1000, N=2880, K=2880, bf16 (BASELINE configs[3], B=1 variant: low tile count)"),
     "T": dict(b=4, m=256, n=512, k=384, dtype="bf16", per_gpu=True,
               desc="T: B=4, M=256, N=512, K=384, bf16 (BASELINE configs[0])"),
     # E's 131072 tokens routed unevenly (Zipf-like expert popularity, seeded), some experts empty

@@ -90,6 +90,7 @@ struct gg_handle {
     int opt_raster = -1;
     int opt_bn = 0;
     int opt_split = 0;
+    int opt_sk_tail = -1;
     int opt_max_ctas = 0;
     int64_t opt_timeout_ms = 2000;
     int opt_test_stall = 0;
@@ -161,40 +162,55 @@ struct Choice {
     int variant;
     int bn;
     int splits;
+    bool hybrid;  // splits > 1: only tiles % slots tiles are split (what would be a partial last wave)
 };
 
-// Model of one launch in cycles per SM: waves x K-atoms x 4 MMAs x cycles per MMA, where one
-// MMA covers 128 rows x bn x 16 per SM. The cycles per MMA are fitted to B200 measurements on a
-// large problem (config L) for each variant and width: the tensor pipe needs bn/2 cycles, but
-// the single issuing thread, the per-stage wait/commit and the L2->SM traffic (which grows as
-// tiles narrow) add a part that shrinks slower than bn. Waves count whole, so the model trades
-// tile width against wave quantisation and M/N tail waste.
-double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots_pairs_or_ctas, int splits) {
+// Cycles per MMA of one CTA (pair) for a tile width, fitted to B200 measurements for each
+// variant: the tensor pipe needs bn/2 cycles, but the single issuing thread, the per-stage
+// wait/commit and the L2->SM traffic add a part that shrinks slower than bn. For the pair
+// variant, timestamps inside the kernel show a floor of ~130 cycles per instruction below a
+// width of ~200 (and ~150 for the one-atom 1-CTA variant): narrower tiles buy little per MMA.
+double cycles_per_mma(const Variant &v, int bn) {
+    if (v.cg == 2)
+        return std::max(0.344 * bn + 60.0, 130.0);
+    return v.atoms >= 2 ? 0.344 * bn + 63.0 : std::max(0.396 * bn + 70.0, 150.0);
+}
+
+// Model of one launch in cycles per SM: waves x K-atoms x 4 MMAs x cycles per MMA. Waves count
+// whole, so the model trades tile width against wave quantisation and M/N tail waste. With
+// splits > 1 every tile (hybrid = false), or only tiles % slots of them (hybrid = true: the
+// tiles that would form a partial last wave), is cut into `splits` K ranges whose fp32
+// partials the last arriving split sums. Split units run first; in the hybrid form the whole
+// tiles that follow hide that fix-up, in the plain form it ends the launch.
+double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots, int splits, bool hybrid) {
     const int64_t tiles = tiles_for(p, v, bn);
-    const int64_t waves = (tiles * splits + slots_pairs_or_ctas - 1) / slots_pairs_or_ctas;
-    const double per_mma = v.cg == 2 ? 0.344 * bn + 60.0 : v.atoms >= 2 ? 0.344 * bn + 63.0 : 0.396 * bn + 70.0;
     const int64_t atoms = (p->k + gg::kBK - 1) / gg::kBK;
-    const int64_t atoms_per_unit = (atoms + splits - 1) / splits;
+    const double per_mma = cycles_per_mma(v, bn);
     // A CTA pair pays a fixed start-up cost (cluster barrier, cross-CTA pipeline fill) that only
     // matters for launches of a few microseconds.
     double fixed = v.cg == 2 ? 1500.0 : 0.0;
-    if (splits > 1) {
-        // split-K: fp32 partials written by every split and read back by the last one
-        int64_t total_m = 0;
-        for (int g = 0; g < p->group_num; ++g)
-            total_m += p->group_m[g];
-        const double bytes = 2.0 * double(splits) * double(total_m) * double(p->n) * 4.0;
-        fixed += 3000.0 + bytes / 2000.0;  // ~2 KB per SM-clock of L2/HBM bandwidth, whole GPU
+    double unit_atoms;
+    if (splits <= 1) {
+        unit_atoms = double((tiles + slots - 1) / slots) * double(atoms);
+    } else {
+        const int64_t whole = hybrid ? tiles / slots * slots : 0;
+        const int64_t split_units = (tiles - whole) * splits;
+        unit_atoms = double(whole / slots) * double(atoms) +
+                     double((split_units + slots - 1) / slots) * double((atoms + splits - 1) / splits);
+        // fix-up: each split writes its fp32 partial (128 x bn per CTA), the last arriver reads
+        // the others back and stores out with direct stores
+        fixed += hybrid ? 1000.0 + double(splits - 1) * double(bn) * 12.0 : 2500.0 + double(splits) * double(bn) * 10.0;
     }
-    return double(waves) * double(atoms_per_unit) * 4.0 * per_mma + fixed;
+    return unit_atoms * 4.0 * per_mma + fixed;
 }
 
-// Pick the variant and tile width with the smallest modelled time. `forced_variant` >= 0 and
-// `forced_bn` > 0 restrict the search. `pairs` is the number of co-resident CTA pairs of the
-// 2-CTA variant.
+// Pick the variant, tile width and split-K form with the smallest modelled time.
+// `forced_variant` >= 0 and `forced_bn` > 0 restrict the search; `min_splits`..`max_splits` is
+// the range of split counts tried; `forced_hybrid` is -1 (either form), 0 or 1. `pairs` is the
+// number of co-resident CTA pairs of the 2-CTA variant.
 Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_variant, int forced_bn,
-                     int max_splits = 1, bool mn_major_b = false) {
-    Choice best{-1, 0, 1};
+                     int max_splits = 1, bool mn_major_b = false, int min_splits = 1, int forced_hybrid = -1) {
+    Choice best{-1, 0, 1, false};
     double best_t = 0;
     const int64_t atoms = (p->k + gg::kBK - 1) / gg::kBK;
     for (int vi = 0; vi < 3; ++vi) {
@@ -212,14 +228,26 @@ Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_var
             if (mn_major_b && (bn / v.cg) % 64 != 0)
                 continue;  // MN-major B is loaded in 64-column boxes
             const int64_t tiles = tiles_for(p, v, bn);
-            for (int s = 1; s <= max_splits; ++s) {
-                // split only below one full wave, and only with >= 8 K atoms per split
-                if (s > 1 && (tiles >= slots || atoms < 8 * s || tiles * s > 4 * int64_t(slots)))
-                    break;
-                const double t = model_cycles(p, v, bn, slots, s);
-                if (best.variant < 0 || t < best_t * 0.999) {
-                    best = {vi, bn, s};
-                    best_t = t;
+            for (int s = min_splits; s <= max_splits; ++s) {
+                for (int hy = 0; hy < 2; ++hy) {
+                    if ((s == 1 && hy == 1) || (forced_hybrid >= 0 && s > 1 && hy != forced_hybrid))
+                        continue;
+                    const bool forced = min_splits > 1;
+                    if (s > 1 && !forced) {
+                        // automatic split-K: >= 8 K atoms per split, and the split units of the
+                        // pure form fill at most 4 waves, those of the hybrid form 2
+                        const int64_t rem = hy ? tiles % slots : tiles;
+                        if (atoms < 8 * s || rem == 0 || (hy && tiles < slots) || (!hy && tiles >= slots) ||
+                            rem * s > (hy ? 2 : 4) * int64_t(slots))
+                            continue;
+                    }
+                    if (s > 1 && hy && tiles % slots == 0)
+                        continue;  // no partial wave to split
+                    const double t = model_cycles(p, v, bn, slots, s, hy == 1);
+                    if (best.variant < 0 || t < best_t * 0.999) {
+                        best = {vi, bn, s, hy == 1};
+                        best_t = t;
+                    }
                 }
             }
         }
@@ -262,6 +290,10 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < 0 || value > 8)
             return fail(h, GG_ERR_ARG, "split must be 0 (auto) or 1..8");
         h->opt_split = int(value);
+    } else if (!std::strcmp(key, "split_tail")) {
+        if (value < -1 || value > 1)
+            return fail(h, GG_ERR_ARG, "split_tail must be -1 (auto), 0 (split every tile) or 1 (only the last wave)");
+        h->opt_sk_tail = int(value);
     } else if (!std::strcmp(key, "bn")) {
         if (value != 0 && (value < 32 || value > 256 || value % 32 != 0))
             return fail(h, GG_ERR_ARG, "bn must be 0 (auto) or a multiple of 32 in 32..256");
@@ -479,17 +511,15 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
         max_splits = h->opt_split > 0 ? h->opt_split : 1;
     if (op == gg::kOpWgrad)
         max_splits = 1;
-    Choice ch = choose_tiling(&cm, num_sms, pairs, h->opt_variant, h->opt_bn, max_splits, mn_b);
-    if (h->opt_split > 0 && ch.variant >= 0 && op != gg::kOpWgrad) {
-        // forced split count: keep the chosen tiling, use exactly that many splits
-        const int64_t atoms = (cm.k + gg::kBK - 1) / gg::kBK;
-        if (h->opt_split > atoms)
-            return refuse(h, why, why_len, "split exceeds the number of 64-wide K atoms");
-        ch.splits = h->opt_split;
-    }
+    if (h->opt_split > 1 && h->opt_split > (cm.k + gg::kBK - 1) / gg::kBK)
+        return refuse(h, why, why_len, "split exceeds the number of 64-wide K atoms");
+    // a forced split count is used exactly (the tiling is chosen for it)
+    const Choice ch = choose_tiling(&cm, num_sms, pairs, h->opt_variant, h->opt_bn, max_splits, mn_b,
+                                    h->opt_split > 1 && op != gg::kOpWgrad ? h->opt_split : 1, h->opt_sk_tail);
     if (ch.variant < 0)
         return refuse(h, why, why_len,
-                      mn_b && h->opt_bn > 0 ? "bn must be a multiple of 64 per CTA for a backward operation"
+                      mn_b && h->opt_bn > 0    ? "bn must be a multiple of 64 per CTA for a backward operation"
+                      : h->opt_sk_tail == 1 ? "split_tail=1: this tiling has no partial last wave to split"
                                             : "no kernel variant fits this device and these options");
     const int vi = ch.variant;
     const int bn = ch.bn;
@@ -510,6 +540,11 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     }
     meta[G] = int32_t(tiles);
     meta[2 * G + 1] = int32_t(rows);
+    // Split-K form: every tile split, or (hybrid) only as many tiles as would form a partial last
+    // wave; the split tiles' units run first, the whole tiles after them.
+    const int64_t clusters = std::max(1, v.cg == 2 ? pairs : num_sms);
+    const int64_t split_tiles = ch.splits > 1 ? (ch.hybrid ? tiles % clusters : tiles) : 0;
+    const int64_t units = tiles + split_tiles * (ch.splits - 1);
 
     if (h->meta_cap < meta.size()) {
         if (h->d_meta)
@@ -523,9 +558,9 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
         GG_CUDA(h, cudaMalloc(&h->d_status, 16));
     GG_CUDA(h, cudaMemsetAsync(h->d_status, 0, 16, stream));
     if (ch.splits > 1) {
-        // tile-private partials: per tile and CTA, 128 rows x bn fp32 per split
-        const size_t ws_bytes = size_t(tiles) * size_t(v.cg) * size_t(ch.splits) * 128 * size_t(bn) * sizeof(float);
-        const size_t ctr_bytes = size_t(tiles) * size_t(v.cg) * 4 * sizeof(int32_t);
+        // tile-private partials: per split tile and CTA, 128 rows x bn fp32 per split
+        const size_t ws_bytes = size_t(split_tiles) * size_t(v.cg) * size_t(ch.splits) * 128 * size_t(bn) * sizeof(float);
+        const size_t ctr_bytes = size_t(split_tiles) * size_t(v.cg) * 4 * sizeof(int32_t);
         if (h->ws_cap < ws_bytes) {
             if (h->d_ws)
                 cudaFree(h->d_ws);
@@ -612,7 +647,7 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     const int slots = v.cg == 2 ? 2 * pairs : num_sms;  // CTAs that can be resident at once
     if (slots < v.cg)
         return refuse(h, why, why_len, "no CTA of this kernel fits on the device");
-    const int64_t want = tiles * ch.splits * v.cg;
+    const int64_t want = units * v.cg;
     h->grid = int(std::max<int64_t>(v.cg, std::min<int64_t>(slots, want)));
 
     gg::KernelParams &kp = h->params;
@@ -631,6 +666,7 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     kp.bn = bn;
     kp.total_tiles = int32_t(tiles);
     kp.splits = ch.splits;
+    kp.split_tiles = int32_t(split_tiles);
     kp.ws = ch.splits > 1 ? h->d_ws : nullptr;
     kp.counters = ch.splits > 1 ? h->d_counters : nullptr;
     kp.band = band;
@@ -650,9 +686,10 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     h->cg = v.cg;
     char d[256];
     std::snprintf(d, sizeof(d),
-                  "gg_sm100<%s%s%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld split=%d grid=%d band=%d%s",
+                  "gg_sm100<%s%s%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld split=%d%s grid=%d band=%d%s",
                   q.dtype == GG_BF16 ? "bf16" : "fp16", op == gg::kOpForward ? "" : ",", op == gg::kOpForward ? "" : op_name(op),
-                  v.cluster_m, bn, gg::kBK * v.atoms, v.cg, v.stages, (long long)tiles, ch.splits, h->grid, band,
+                  v.cluster_m, bn, gg::kBK * v.atoms, v.cg, v.stages, (long long)tiles, ch.splits,
+                  split_tiles > 0 && split_tiles < tiles ? "(last wave)" : "", h->grid, band,
                   raster ? "n" : "");
     h->detail = d;
     h->ready = true;

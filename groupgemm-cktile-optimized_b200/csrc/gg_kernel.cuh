@@ -93,9 +93,10 @@ struct KernelParams {
     int32_t tiles_n;      // ceil(N / bn)
     int32_t bn;           // tile N of this launch: a multiple of 32, <= the variant's kBN
     int32_t total_tiles;  // tile_off[G]
-    int32_t splits;       // K splits per tile (0 or 1 = none); work units = total_tiles x splits
-    float *ws;            // splits > 1: fp32 partial sums, per tile [kCG][4 warps][splits][bn/32] 4-KB blocks
-    int32_t *counters;    // splits > 1: [total_tiles][kCG][4] arrival counts, 0 between launches
+    int32_t splits;       // K splits of each split tile (0 or 1 = none)
+    int32_t split_tiles;  // splits > 1: tiles [0, split_tiles) are split in `splits`, the rest run whole
+    float *ws;            // splits > 1: fp32 partial sums, per split tile [kCG][4 warps][splits][bn/32] 4-KB blocks
+    int32_t *counters;    // splits > 1: [split tiles][kCG][4] arrival counts, 0 between launches
     int32_t band;         // tiles per raster band (L2 reuse, see decode_tile)
     int32_t raster;       // 0: bands of `band` m-tiles, n-tiles swept; 1: bands of `band` n-tiles
     int32_t test_stall;   // test only: 1 = the first stage of cluster 0 is never loaded, so the
@@ -191,6 +192,25 @@ __device__ __forceinline__ TileCoord decode_tile(const KernelParams &p, int t, i
         tc.nt = b * p.band + (r - tc.mt * cols);
     }
     return tc;
+}
+
+// A work unit: a whole tile, or one K split of a split tile. Units [0, split_tiles x splits) are
+// the splits of tiles [0, split_tiles), scheduled first so that the split-K fix-up (partials
+// written, the last arriver's reduction) runs in the epilogue warps while the MMA warp works on
+// the whole tiles that follow; then one unit per remaining tile. split_tiles = total_tiles is
+// plain split-K; fewer split tiles is split-K for what would otherwise be a partial last wave.
+struct Unit {
+    int t, split, nsplit;
+};
+__device__ __forceinline__ Unit unit_of(const KernelParams &p, int u) {
+    const int s = p.splits > 1 ? p.splits : 1;
+    if (s == 1)
+        return {u, 0, 1};
+    if (u < p.split_tiles * s) {
+        const int q = u / s;
+        return {q, u - q * s, s};
+    }
+    return {u - p.split_tiles * (s - 1), 0, 1};
 }
 
 struct Abort {
@@ -335,6 +355,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_ptr_slot;
     // Everything above is on-chip set-up. With programmatic dependent launch it overlaps the
     // previous kernel's tail; global memory is touched only after this wait.
+    // The group-offset table is written by the host before the stream reaches this launch, never
+    // by a preceding kernel, so the first tile's look-up may run before the dependency wait: it
+    // brings the table's first lines into this SM's cache while the previous kernel finishes.
+    if (threadIdx.x == 0) {
+        int cur = 0;
+        const TileCoord tc0 = decode_tile<C::kClusterM, kOp>(p, unit_of(p, cluster_id).t, cur);
+        tmem_ptr_slot[2] = uint32_t(tc0.g + tc0.rows);  // keeps the loads (slot otherwise unused)
+    }
     ptx::griddep_wait();
     ptx::griddep_launch_dependents();
 
@@ -343,9 +371,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // range of K atoms; each unit runs the same producer/MMA/epilogue pipeline over its range.
     // (wgrad runs unsplit: its reduction length differs per group.)
     const int splits = p.splits > 1 ? p.splits : 1;
-    const int total_units = p.total_tiles * splits;
-    // Split i covers K atoms [i * num_kb / splits, (i + 1) * num_kb / splits): balanced, and never
-    // empty while splits <= num_kb (the host refuses more splits than atoms).
+    const int total_units = p.total_tiles + p.split_tiles * (splits - 1);
+    // Split i of n covers K atoms [i * num_kb / n, (i + 1) * num_kb / n): balanced, and never empty
+    // while n <= num_kb (the host refuses more splits than atoms).
 
     if (warp == 0) {
         // ---------------- TMA producer (one thread) ----------------
@@ -357,10 +385,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             int fenced_g = -1;  // wgrad: group whose tensor maps this thread has acquired
             for (int u = cluster_id; u < total_units && ok; u += num_clusters) {
-                const int t = u / splits;
-                const TileCoord tc = decode_tile<C::kClusterM, kOp>(p, t, cursor);
-                const int atom0 = kOp == kOpWgrad ? 0 : (u - t * splits) * p.num_kb / splits;
-                const int atom1 = kOp == kOpWgrad ? tc.red_atoms : (u - t * splits + 1) * p.num_kb / splits;
+                const Unit un = unit_of(p, u);
+                const TileCoord tc = decode_tile<C::kClusterM, kOp>(p, un.t, cursor);
+                const int atom0 = kOp == kOpWgrad ? 0 : un.split * p.num_kb / un.nsplit;
+                const int atom1 = kOp == kOpWgrad ? tc.red_atoms : (un.split + 1) * p.num_kb / un.nsplit;
                 const int num_ks = (atom1 - atom0 + kAtoms - 1) / kAtoms;
                 // A: first row (forward/dgrad: token row; wgrad: row of dw[g], a column of dy)
                 const int a_row = (kOp == kOpWgrad ? 0 : tc.out_row0) + tc.mt * C::kClusterM + int(cta_rank) * kBM;
@@ -444,11 +472,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int atom0, atom1;
                 if constexpr (kOp == kOpWgrad) {
                     atom0 = 0;
-                    atom1 = decode_tile<C::kClusterM, kOp>(p, u / splits, cursor).red_atoms;  // 0 for an empty group
+                    atom1 = decode_tile<C::kClusterM, kOp>(p, u, cursor).red_atoms;  // 0 for an empty group
                 } else {
-                    const int sp = u - (u / splits) * splits;
-                    atom0 = sp * p.num_kb / splits;
-                    atom1 = (sp + 1) * p.num_kb / splits;
+                    const Unit un = unit_of(p, u);
+                    atom0 = un.split * p.num_kb / un.nsplit;
+                    atom1 = (un.split + 1) * p.num_kb / un.nsplit;
                 }
                 const int num_ks = (atom1 - atom0 + kAtoms - 1) / kAtoms;
                 const int acc = int(tl & 1u);
@@ -520,8 +548,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         int cursor = 0;
         uint32_t tl = 0;
         for (int u = cluster_id; u < total_units; u += num_clusters, ++tl) {
-            const int t = u / splits;
-            const int split = u - t * splits;
+            const Unit un = unit_of(p, u);
+            const int t = un.t;
+            const int split = un.split;
+            const int nsplit = un.nsplit;
             const TileCoord tc = decode_tile<C::kClusterM, kOp>(p, t, cursor);
             const int acc = int(tl & 1u);
             const uint32_t acc_ph = (tl >> 1) & 1u;
@@ -539,9 +569,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * kBN);
             bool store_out = true;
             const int nch = bn / 32;  // 32-column chunks of the tile
-            // split-K: first float4 of this warp's workspace region (splits x nch blocks of 4 KB)
-            const int64_t ws_warp = ((int64_t(t) * kCG + int(cta_rank)) * 4 + q) * int64_t(splits) * nch * 256;
-            if (splits > 1) {
+            // split-K: first float4 of this warp's workspace region (nsplit x nch blocks of 4 KB)
+            const int64_t ws_warp = ((int64_t(t) * kCG + int(cta_rank)) * 4 + q) * int64_t(nsplit) * nch * 256;
+            if (nsplit > 1) {
                 // Split-K: publish this unit's fp32 partial; the last of the tile's splits to
                 // arrive (per CTA and warp) sums all of them in split order and stores out.
                 // This warp's workspace blocks of the tile: [split][chunk], each block the 32 x 32
@@ -566,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0)
                     prev = atomicAdd(ctr, 1);
                 prev = __shfl_sync(0xffffffffu, prev, 0);
-                store_out = prev == splits - 1;
+                store_out = prev == nsplit - 1;
                 if (store_out) {
                     __threadfence();
                     if (lane == 0)
@@ -576,18 +606,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             // TMA-store path: the warp's 32 rows all inside the group and no split-K sums; each
             // pair of 32-column chunks goes out as one 64 x 32 box through a staging buffer.
             const int slab_rows_ok = m - (tc.mt * C::kClusterM + int(cta_rank) * kBM + q * 32);
-            const int c_tma = (GG_TMA_STORE && splits == 1 && slab_rows_ok >= 32) ? (bn / 64) * 2 : 0;
+            const int c_tma = (GG_TMA_STORE && nsplit == 1 && slab_rows_ok >= 32) ? (bn / 64) * 2 : 0;
 #pragma unroll 1
             for (int c = 0; c < c_tma; c += 2) {
                 const uint32_t buf = out_stage + uint32_t(out_buf) * C::kStageOutBytes;
                 if (lane == 0)
                     ptx::bulk_wait_group_read<1>();  // this buffer's previous store has read it
                 __syncwarp();
+                // both 32-column halves of the box in flight before one wait
+                uint32_t rr[2][32];
+                ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), rr[0]);
+                ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + 1) * 32), rr[1]);
+                ptx::tmem_wait_ld(rr[0]);
+                ptx::tmem_tie(rr[1]);
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
-                    uint32_t r[32];
-                    ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + hh) * 32), r);
-                    ptx::tmem_wait_ld(r);
+                    uint32_t (&r)[32] = rr[hh];
                     if (zero_tile) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j)
@@ -612,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // Split-K reduction by the last arriver: the other splits' blocks are read in (chunk,
             // split) order with one block always in flight ahead of the one being added.
-            const int others = splits - 1;
+            const int others = nsplit - 1;
             auto other_blk = [&](int idx) {
                 const int c = idx / others;
                 const int o = idx - c * others;
@@ -621,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             };
             float4 nxt[8];
             int blk = 0;
-            if (store_out && splits > 1) {
+            if (store_out && nsplit > 1) {
                 const float4 *src = other_blk(0);
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
@@ -638,13 +672,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         r[j] = 0u;
                 }
                 const int col = tc.nt * bn + c * 32;
-                if (splits > 1) {
-                    // r = sum over splits 0..splits-1 in that order; this unit's own part from TMEM
+                if (nsplit > 1) {
+                    // r = sum over splits 0..nsplit-1 in that order; this unit's own part from TMEM
                     float sum[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
                         sum[j] = 0.f;
-                    for (int s2 = 0; s2 < splits; ++s2) {
+                    for (int s2 = 0; s2 < nsplit; ++s2) {
                         if (s2 == split) {
 #pragma unroll
                             for (int j = 0; j < 32; ++j)

@@ -325,3 +325,52 @@ def test_split_k_more_splits_than_atom_pairs(gg, orc, variant, split):
     assert np.all(res[sum(group_m) * n:] == CANARY)
     bad, mx, first = orc.check16(res[: sum(group_m) * n].reshape(-1, n), ref, 0)
     assert bad == 0, (b.detail(), bad, mx, first)
+
+
+@pytest.mark.parametrize("variant,bn", [(0, 256), (1, 256), (2, 128)])
+@pytest.mark.parametrize("split", [2, 3])
+def test_split_k_last_wave_only(gg, orc, variant, bn, split):
+    """Hybrid split-K: the grid is capped at 10 CTAs so the tiles form whole waves plus a partial
+    one; whole waves run unsplit (TMA-store epilogue), the last wave's tiles are split in K (fp32
+    partials, last-arriver reduction). Two launches in a row reuse the arrival counters."""
+    torch = _torch()
+    group_m, n, k = [300, 0, 17, 513], 1000, 1000
+    x, w = orc.make_inputs(group_m, n, k, 0)
+    ref = orc.grouped_gemm_f32(x, w, group_m, 0)
+    xd, wd = upload(torch, x), upload(torch, w)
+    total = sum(group_m)
+    out = torch.full((total * n + GUARD,), CANARY, dtype=torch.int16, device="cuda")
+    b = gg.B200Backend()
+    for key, val in (("variant", variant), ("bn", bn), ("split", split), ("split_tail", 1), ("max_ctas", 10)):
+        b.set_option(key, val)
+    s = torch.cuda.current_stream().cuda_stream
+    assert b.prepare(0, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s) == ""
+    assert f"split={split}(last wave)" in b.detail(), b.detail()
+    for _ in range(2):
+        out[:total * n].fill_(0)
+        b.run(s)
+        assert b.device_status(s) == 0
+        res = out.cpu().numpy().view(np.uint16)
+        assert np.all(res[total * n:] == CANARY)
+        bad, mx, first = orc.check16(res[:total * n].reshape(-1, n), ref, 0)
+        assert bad == 0, (b.detail(), bad, mx, first)
+
+
+def test_dgrad_split_k_last_wave_only(gg, orc):
+    torch = _torch()
+    group_m, n, k = [300, 0, 17, 513], 1000, 1024
+    dy, x, w = orc.make_grad_inputs(group_m, n, k, 0)
+    ref = orc.grouped_dgrad_f32(dy, w, group_m, 0)
+    dyd, wd = upload(torch, dy), upload(torch, w)
+    dx = torch.zeros(sum(group_m) * k, dtype=torch.int16, device="cuda")
+    b = gg.B200Backend()
+    for key, val in (("variant", 0), ("bn", 256), ("split", 2), ("split_tail", 1), ("max_ctas", 10)):
+        b.set_option(key, val)
+    s = torch.cuda.current_stream().cuda_stream
+    assert b.prepare_grad(gg.OP_DGRAD, 0, group_m, n, k, dy_ptr=dyd.data_ptr(), w_ptr=wd.data_ptr(),
+                          dx_ptr=dx.data_ptr(), stream=s) == ""
+    assert "(last wave)" in b.detail(), b.detail()
+    b.run(s)
+    assert b.device_status(s) == 0
+    bad, mx, first = orc.check16(dx.cpu().numpy().view(np.uint16).reshape(-1, k), ref, 0)
+    assert bad == 0, (b.detail(), bad, mx, first)
