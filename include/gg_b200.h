@@ -130,11 +130,17 @@ const char *gg_last_error(const gg_handle *h);
  * out (its only device-side guard is a trap, ck_kernel/fast_epilogue.hpp:38-41). */
 int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
 
-/* Override the automatic choices of gg_prepare (takes effect at the next gg_prepare):
+/* Override the automatic choices of gg_prepare / gg_prepare_grad (takes effect at the next
+ * prepare):
  *   "variant"    -1 auto, 0 = 2-CTA 256x256 tile, 1 = 1-CTA 128x256, 2 = 1-CTA 128x128
- *   "band"       M tiles per raster band (default chosen per shape), 0 = auto
+ *   "band"       tiles per raster band (default chosen per shape), 0 = auto
+ *   "raster"     -1 auto (= 0), 0 = bands of M tiles (weight panels shared), 1 = bands of N tiles
  *   "bn"         tile width (multiple of 32, <= the variant's), 0 = auto (cost model)
- *   "split"      K splits per tile (split-K with an fp32 workspace), 0 = auto, 1 = none
+ *   "split"      K splits per split tile (split-K with an fp32 workspace), 0 = auto, 1 = none
+ *   "split_tail" -1 auto, 0 = split every tile, 1 = split only the tiles of what would be a
+ *                partial last wave (their units run first, whole tiles after them)
+ *   "pdl"        1 (default) = launch with programmatic stream serialisation, so the launch and
+ *                on-chip set-up overlap the previous kernel in the stream; 0 = plain launch
  *   "max_ctas"   cap on the persistent grid (0 = one CTA per SM)
  *   "timeout_ms" bounded-wait limit inside the kernel (default 2000)
  *   "test_stall" test only: 1 = the kernel never loads the first stage of its first CTA (pair),
