@@ -547,6 +547,14 @@ def main():
                 "kernel": "gg::grouped_gemm_sm100 (" + backend.detail() + ")"}
     if traffic:
         roofline["traffic_source"] = traffic.get("source")
+    # the memory side of the same launch: algorithmic bytes (and measured DRAM traffic, where a
+    # capture exists) per launch time against the measured copy bandwidth
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK["hbm_gbs"]))
+    alg_gbs = roofline["algorithmic_bytes"] / (ms_step_rank * 1e-3) / 1e9
+    roofline["hbm"] = {"algorithmic_gbs": round(alg_gbs, 1), "peak_gbs": hbm_peak,
+                       "frac_algorithmic": round(alg_gbs / hbm_peak, 4),
+                       "traffic_gbs": round(traffic["bytes_per_launch"] / (ms_step_rank * 1e-3) / 1e9, 1)
+                       if traffic else None}
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak"

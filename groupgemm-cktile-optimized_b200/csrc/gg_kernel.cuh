@@ -11,17 +11,22 @@
 // ck_kernel/fast_epilogue.hpp:29-118) with a Blackwell design:
 //
 //   * one CTA per SM (kCG = 1) or one CTA pair per two SMs (kCG = 2, tcgen05 cta_group::2),
-//     persistent over a static tile schedule that covers every group (the scheduler is on the
-//     device: a tile index is mapped to (group, m-tile, n-tile) from per-group tile offsets);
+//     persistent over a static schedule of work units that covers every group (the scheduler
+//     is on the device: a unit is a tile or a K split of one, a tile index is mapped to
+//     (group, m-tile, n-tile) from per-group tile offsets);
 //   * warp 0: TMA producer. 128-byte-swizzled A (128 x 64) and B (BN/kCG x 64) tiles into a
 //     STAGES-deep shared-memory ring guarded by full/empty mbarriers (no multicast: every CTA
 //     loads its own halves);
 //   * warp 1: TMEM allocator and, in the pair leader, the single MMA-issuing thread. The
 //     accumulator lives in Tensor Memory, double-buffered (2 x BN fp32 columns) so the
 //     epilogue of tile i overlaps the main loop of tile i+1;
-//   * warps 2-5: epilogue. tcgen05.ld 32 lanes x 32 columns, fp32 -> bf16/fp16 (RNE),
-//     row/column-masked 16-byte streaming stores (evict-first, the analogue of the
-//     reference's non-temporal C stores, ck_kernel/coherence_epilogue.hpp:17-30).
+//   * warps 2-5: epilogue. tcgen05.ld 32 lanes x 32 columns, fp32 -> bf16/fp16 (RNE), then
+//     per warp 32-row x 64-column boxes through 128-byte-swizzled shared-memory staging and TMA
+//     stores with an evict-first L2 policy (the analogue of the reference's non-temporal C
+//     stores, ck_kernel/coherence_epilogue.hpp:17-30); slabs that cross a group's end, column
+//     tails and split-K sums use masked 32-byte streaming stores;
+//   * launched with programmatic stream serialisation: on-chip set-up overlaps the previous
+//     kernel, global memory is touched only after griddepcontrol.wait.
 //
 // Tails: TMA zero-fills reads past the tensor ends (K tail, N tail via the 3-D weight map,
 // rows past sum(M)). A tile that runs past its group's last row reads the next group's rows;

@@ -166,3 +166,39 @@ def test_forward_after_backward_on_one_handle(gg, orc):
     assert orc.check16(dw.cpu().numpy().view(np.uint16).reshape(-1, k), ref_dw, 0)[0] == 0
     ref = orc.grouped_gemm_f32(x, w, group_m, 0)
     assert orc.check16(out.cpu().numpy().view(np.uint16).reshape(-1, n), ref, 0)[0] == 0
+
+
+@pytest.mark.parametrize("name", OPS)
+def test_config_l_size_two_experts_vs_torch_fp32(gg, name):
+    """BASELINE config L's shape (B=8, M=4096, N=4096, K=7168, bf16): the whole output of the
+    first and the last expert against a torch fp32 matmul of the same bf16 inputs."""
+    torch = _torch()
+    B, M, N, K = 8, 4096, 4096, 7168
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    dy = torch.randn(B * M, N, device="cuda", generator=gen).to(torch.bfloat16)
+    group_m = [M] * B
+    s = torch.cuda.current_stream().cuda_stream
+    b = gg.B200Backend()
+    if name == "dgrad":
+        w = torch.randn(B, N, K, device="cuda", generator=gen).to(torch.bfloat16)
+        dx = torch.empty(B * M, K, device="cuda", dtype=torch.bfloat16)
+        assert b.prepare_grad(gg.OP_DGRAD, gg.BF16, group_m, N, K, dy_ptr=dy.data_ptr(), w_ptr=w.data_ptr(),
+                              dx_ptr=dx.data_ptr(), stream=s) == ""
+    else:
+        x = torch.randn(B * M, K, device="cuda", generator=gen).to(torch.bfloat16)
+        dw = torch.empty(B, N, K, device="cuda", dtype=torch.bfloat16)
+        assert b.prepare_grad(gg.OP_WGRAD, gg.BF16, group_m, N, K, dy_ptr=dy.data_ptr(), x_ptr=x.data_ptr(),
+                              dw_ptr=dw.data_ptr(), stream=s) == ""
+    b.run(s)
+    assert b.device_status(s) == 0
+    for g in (0, B - 1):
+        rows = slice(g * M, (g + 1) * M)
+        if name == "dgrad":
+            ref = dy[rows].float() @ w[g].float()
+            got = dx[rows].float()
+        else:
+            ref = dy[rows].float().t() @ x[rows].float()
+            got = dw[g].float()
+        bad = ((got - ref).abs() > 1e-2 + 1e-2 * ref.abs()) | torch.isnan(got)
+        assert int(bad.sum()) == 0, (name, g, int(bad.sum()), float((got - ref).abs().max()))
+    b.release()
