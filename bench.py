@@ -49,6 +49,10 @@ CONFIGS = {
               desc="P: B=16 experts per GPU, M=1000, N=2880, K=2880, bf16 (BASELINE configs[3])"),
     "P1": dict(b=1, m=1000, n=2880, k=2880, dtype="bf16", per_gpu=True,
                desc="P1: B=1 expert, M=1000, N=2880, K=2880, bf16 (BASELINE configs[3], B=1 variant: low tile count)"),
+    # synthetic: 2 x 2 x 24 = 96 pair tiles for 74 CTA pairs, a partial last wave (split-K of the
+    # last wave only)
+    "W": dict(b=2, m=512, n=6144, k=8192, dtype="bf16", per_gpu=True,
+              desc="W: synthetic B=2, M=512, N=6144, K=8192, bf16 (96 pair tiles on 74 pairs: a partial last wave)"),
     "T": dict(b=4, m=256, n=512, k=384, dtype="bf16", per_gpu=True,
               desc="T: B=4, M=256, N=512, K=384, bf16 (BASELINE configs[0])"),
     # E's 131072 tokens routed unevenly (Zipf-like expert popularity, seeded), some experts empty
