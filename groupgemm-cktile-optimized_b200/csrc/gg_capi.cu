@@ -95,6 +95,7 @@ struct gg_handle {
     int64_t opt_timeout_ms = 2000;
     int opt_test_stall = 0;
     int opt_pdl = 1;
+    int opt_store = -1;  // -1 auto, 0 = staging + TMA stores, 1 = direct stores
 
     // prepared state
     bool ready = false;
@@ -306,6 +307,10 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < 1 || value > 60000)
             return fail(h, GG_ERR_ARG, "timeout_ms must be 1..60000");
         h->opt_timeout_ms = value;
+    } else if (!std::strcmp(key, "store")) {
+        if (value < -1 || value > 1)
+            return fail(h, GG_ERR_ARG, "store must be -1 (auto), 0 (TMA stores) or 1 (direct stores)");
+        h->opt_store = int(value);
     } else if (!std::strcmp(key, "pdl")) {
         if (value != 0 && value != 1)
             return fail(h, GG_ERR_ARG, "pdl must be 0 or 1");
@@ -671,6 +676,8 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     kp.counters = ch.splits > 1 ? h->d_counters : nullptr;
     kp.band = band;
     kp.raster = raster;
+    // epilogue store path: direct stores for tiles with >= 16 K atoms (1024 of reduction)
+    kp.store_min_atoms = h->opt_store == 0 ? (1 << 30) : h->opt_store == 1 ? 0 : 16;
     kp.test_stall = h->opt_test_stall;
     kp.timeout_ns = uint64_t(h->opt_timeout_ms) * 1000000ull;
 
@@ -986,33 +993,16 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
 
     const CUtensorMapDataType dt =
         p->dtype == GG_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    CUtensorMap tmap_a, tmap_b;
-    const cuuint32_t estride[3] = {1, 1, 1};
-    const cuuint64_t a_dim[2] = {cuuint64_t(p->k), cuuint64_t(total_m)};
-    const cuuint64_t a_stride[1] = {cuuint64_t(p->k) * 2};
-    const cuuint32_t a_box[2] = {gg::kBK, gg::kBM};
-    if (encode(&tmap_a, dt, 2, const_cast<void *>(p->x), a_dim, a_stride, a_box, estride,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+    CUtensorMap tmap_a, tmap_b, tmap_out;
+    if (encode_2d(encode, &tmap_a, dt, p->x, p->k, total_m, gg::kBK, gg::kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)) {
         copy_msg(why, why_len, "cuTensorMapEncodeTiled(x) failed");
         return GG_ERR_CUDA;
     }
-    const cuuint64_t b_dim[3] = {cuuint64_t(p->k), cuuint64_t(p->n), cuuint64_t(G)};
-    const cuuint64_t b_stride[2] = {cuuint64_t(p->k) * 2, cuuint64_t(p->n) * cuuint64_t(p->k) * 2};
-    const cuuint32_t b_box[3] = {gg::kBK, cuuint32_t(bn / v.cg), 1};
-    if (encode(&tmap_b, dt, 3, const_cast<void *>(p->w), b_dim, b_stride, b_box, estride,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+    if (encode_w(encode, &tmap_b, dt, p->w, p->n, p->k, G, gg::kBK, uint32_t(bn / v.cg))) {
         copy_msg(why, why_len, "cuTensorMapEncodeTiled(w) failed");
         return GG_ERR_CUDA;
     }
-    CUtensorMap tmap_out;
-    const cuuint64_t o_dim[2] = {cuuint64_t(p->n), cuuint64_t(total_m)};
-    const cuuint64_t o_stride[1] = {cuuint64_t(p->n) * 2};
-    const cuuint32_t o_box[2] = {64, 32};
-    if (encode(&tmap_out, dt, 2, p->out, o_dim, o_stride, o_box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+    if (encode_2d(encode, &tmap_out, dt, p->out, p->n, total_m, 64, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE)) {
         copy_msg(why, why_len, "cuTensorMapEncodeTiled(out) failed");
         return GG_ERR_CUDA;
     }
@@ -1030,6 +1020,7 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
     kp.bn = bn;
     kp.total_tiles = int32_t(tiles);
     kp.band = v.cg == 2 ? 8 : 16;
+    kp.store_min_atoms = 16;  // the same epilogue store policy as gg_run's default
     kp.timeout_ns = 2000ull * 1000000ull;
 
     const int slots = v.cg == 2 ? 2 * d->clusters_v0 : d->num_sms;

@@ -139,6 +139,8 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
  *   "split"      K splits per split tile (split-K with an fp32 workspace), 0 = auto, 1 = none
  *   "split_tail" -1 auto, 0 = split every tile, 1 = split only the tiles of what would be a
  *                partial last wave (their units run first, whole tiles after them)
+ *   "store"      -1 auto (direct stores from registers for tiles with >= 16 K atoms, staging +
+ *                TMA stores for shorter ones), 0 = always TMA stores, 1 = always direct stores
  *   "pdl"        1 (default) = launch with programmatic stream serialisation, so the launch and
  *                on-chip set-up overlap the previous kernel in the stream; 0 = plain launch
  *   "max_ctas"   cap on the persistent grid (0 = one CTA per SM)
