@@ -360,11 +360,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::cluster_sync();  // peer barriers are initialised before any remote arrive
     ptx::tc_fence_after();
     const uint32_t tmem_base = *tmem_ptr_slot;
-    // Everything above is on-chip set-up. With programmatic dependent launch it overlaps the
-    // previous kernel's tail; global memory is touched only after this wait.
-    // The group-offset table is written by the host before the stream reaches this launch, never
-    // by a preceding kernel, so the first tile's look-up may run before the dependency wait: it
-    // brings the table's first lines into this SM's cache while the previous kernel finishes.
+    // Everything above is on-chip set-up; with programmatic dependent launch it overlaps the
+    // previous kernel's tail. The group-offset table is written by the host before the stream
+    // reaches this launch (prepare synchronises its stream), never by a preceding kernel, so the
+    // first tile's look-up may also run before the dependency wait, bringing the table's first
+    // lines into this SM's cache meanwhile. Every other global access comes after the wait.
     if (threadIdx.x == 0) {
         int cur = 0;
         const TileCoord tc0 = decode_tile<C::kClusterM, kOp>(p, unit_of(p, cluster_id).t, cur);
@@ -378,9 +378,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::griddep_launch_dependents();
 
     const Abort ab{p.status, abort_flag, p.timeout_ns};
-    // Work units: every tile, or with split-K every (tile, K split). A split covers a contiguous
-    // range of K atoms; each unit runs the same producer/MMA/epilogue pipeline over its range.
-    // (wgrad runs unsplit: its reduction length differs per group.)
+    // Work units (unit_of): the K splits of the split tiles, then the whole tiles. A split covers a
+    // contiguous range of K atoms; each unit runs the same producer/MMA/epilogue pipeline over its
+    // range. (wgrad runs unsplit: its reduction length differs per group.)
     const int splits = p.splits > 1 ? p.splits : 1;
     const int total_units = p.total_tiles + p.split_tiles * (splits - 1);
     // Split i of n covers K atoms [i * num_kb / n, (i + 1) * num_kb / n): balanced, and never empty
