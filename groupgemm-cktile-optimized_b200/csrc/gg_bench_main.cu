@@ -3,6 +3,11 @@
 //
 //   gg_bench --shapes FILE.csv [--dtype bf16|fp16] [--backends b200,cublas_loop,cublas_grouped]
 //            [--only ID,...] [--warmup N] [--iters N] [--no-check] [--out FILE.csv] [--device N]
+//            [--opt KEY=VALUE ...]
+//
+// --opt passes a gg_set_option knob to the b200 backend (variant, bn, split, split_tail, band,
+// raster, store, pdl, max_ctas, timeout_ms): the runtime counterpart of editing the reference's
+// compile-time CkTileConfig (ck_kernel/ck_grouped_gemm_config.hpp:26-86) between runs.
 //
 // Per case (balanced groups: B groups of M rows, like the reference, bench/bench_main.cpp:436):
 // device inputs from the splitmix64 + Box-Muller generator (seeds 1 and 2), output zeroed, then
@@ -47,6 +52,7 @@ struct Options {
     std::set<int> only;
     int warmup = 20, iters = 100, device = 0;
     bool check = true;
+    std::vector<std::pair<std::string, int64_t>> b200_opts;  // --opt KEY=VALUE
 };
 
 std::vector<std::string> split_list(const std::string &s, char sep) {
@@ -65,7 +71,9 @@ std::vector<std::string> split_list(const std::string &s, char sep) {
 [[noreturn]] void die_usage(const std::string &msg) {
     std::cerr << "error: " << msg << "\n"
               << "usage: gg_bench --shapes FILE.csv [--dtype bf16|fp16] [--backends b200,cublas_loop,cublas_grouped]\n"
-              << "                [--only ID,...] [--warmup N] [--iters N] [--no-check] [--out FILE.csv] [--device N]\n";
+              << "                [--only ID,...] [--warmup N] [--iters N] [--no-check] [--out FILE.csv] [--device N]\n"
+              << "                [--opt KEY=VALUE ...]   (b200 knobs: variant, bn, split, split_tail, band, raster,\n"
+              << "                                         store, pdl, max_ctas, timeout_ms)\n";
     std::exit(2);
 }
 
@@ -100,6 +108,17 @@ Options parse(int argc, char **argv) {
             o.device = std::stoi(value());
         else if (a == "--no-check")
             o.check = false;
+        else if (a == "--opt") {
+            const std::string kv = value();
+            const size_t eq = kv.find('=');
+            if (eq == std::string::npos || eq == 0)
+                die_usage("--opt wants KEY=VALUE, got " + kv);
+            try {
+                o.b200_opts.emplace_back(kv.substr(0, eq), std::stoll(kv.substr(eq + 1)));
+            } catch (const std::exception &) {
+                die_usage("--opt value is not an integer: " + kv);
+            }
+        }
         else if (a == "-h" || a == "--help")
             die_usage("help requested");
         else
@@ -342,9 +361,13 @@ void summary(const std::vector<Result> &rows, const std::vector<std::string> &na
     }
 }
 
-std::unique_ptr<gg::Backend> make_backend(const std::string &name) {
-    if (name == "b200")
-        return gg::make_b200_backend();
+std::unique_ptr<gg::Backend> make_backend(const std::string &name, const Options &opt) {
+    if (name == "b200") {
+        auto b = std::make_unique<gg::B200Backend>();
+        for (const auto &kv : opt.b200_opts)
+            b->set_option(kv.first.c_str(), kv.second);  // throws on an unknown key or bad value
+        return b;
+    }
     if (name == "cublas_loop")
         return gg::make_cublas_loop_backend();
     if (name == "cublas_grouped")
@@ -360,7 +383,7 @@ int run(const Options &opt) {
 
     std::vector<std::unique_ptr<gg::Backend>> backends;
     for (const auto &b : opt.backends)
-        backends.push_back(make_backend(b));
+        backends.push_back(make_backend(b, opt));
     std::vector<Case> cases;
     for (const auto &c : load_cases(opt.shapes))
         if (opt.only.empty() || opt.only.count(c.id))
