@@ -5,8 +5,8 @@
 //            [--only ID,...] [--warmup N] [--iters N] [--no-check] [--out FILE.csv] [--device N]
 //            [--opt KEY=VALUE ...]
 //
-// --opt passes a gg_set_option knob to the b200 backend (variant, bn, split, split_tail, band,
-// raster, store, pdl, max_ctas, timeout_ms): the runtime counterpart of editing the reference's
+// --opt passes a gg_set_option knob to the b200 backend (variant, bn, split, split_tail, stream_k,
+// band, raster, store, pdl, max_ctas, timeout_ms): the runtime counterpart of editing the reference's
 // compile-time CkTileConfig (ck_kernel/ck_grouped_gemm_config.hpp:26-86) between runs.
 //
 // Per case (balanced groups: B groups of M rows, like the reference, bench/bench_main.cpp:436):
@@ -73,7 +73,7 @@ std::vector<std::string> split_list(const std::string &s, char sep) {
               << "usage: gg_bench --shapes FILE.csv [--dtype bf16|fp16] [--backends b200,cublas_loop,cublas_grouped]\n"
               << "                [--only ID,...] [--warmup N] [--iters N] [--no-check] [--out FILE.csv] [--device N]\n"
               << "                [--opt KEY=VALUE ...]   (b200 knobs: variant, bn, split, split_tail, band, raster,\n"
-              << "                                         store, pdl, max_ctas, timeout_ms)\n";
+              << "                                         stream_k, store, pdl, max_ctas, timeout_ms)\n";
     std::exit(2);
 }
 

@@ -91,6 +91,8 @@ struct gg_handle {
     int opt_bn = 0;
     int opt_split = 0;
     int opt_sk_tail = -1;
+    int opt_stream_k = 0;  // 0 off (default), -1 cost model decides, 1 / 2 stream-K over the partial
+                           // last wave (+ one wave)
     int opt_max_ctas = 0;
     int64_t opt_timeout_ms = 2000;
     int opt_test_stall = 0;
@@ -164,7 +166,30 @@ struct Choice {
     int bn;
     int splits;
     bool hybrid;  // splits > 1: only tiles % slots tiles are split (what would be a partial last wave)
+    int sk;       // stream-K: 0 none, 1 over the tiles of the partial last wave, 2 over those and
+                  // one full wave more
 };
+
+// Stream-K region of a launch: the first `sk_tiles` tiles, whose K atoms are dealt out evenly to
+// the `clusters` clusters. kind 1: the tiles that would form a partial last wave (tiles % clusters);
+// kind 2: those plus one full wave, so that each cluster's range spans at least one tile. Returns 0
+// when the kind does not apply (no partial wave, too few tiles, or fewer atoms than clusters).
+int64_t sk_tiles_for(int64_t tiles, int64_t clusters, int64_t atoms, int kind) {
+    const int64_t rem = tiles % clusters;
+    const int64_t sk = kind == 1 ? rem : kind == 2 && rem > 0 && tiles >= rem + clusters ? rem + clusters : 0;
+    return sk > 0 && sk * atoms >= clusters ? sk : 0;
+}
+
+// Most pieces any stream-K tile is cut into (cluster c's range is [c S / C, (c+1) S / C)); the
+// kernel's workspace stride and the length of its longest fix-up.
+int sk_max_pieces(int64_t sk_tiles, int64_t clusters, int64_t atoms) {
+    const int64_t S = sk_tiles * atoms;
+    auto cluster_of = [&](int64_t g) { return ((g + 1) * clusters - 1) / S; };
+    int64_t most = 1;
+    for (int64_t t = 0; t < sk_tiles; ++t)
+        most = std::max(most, cluster_of((t + 1) * atoms - 1) - cluster_of(t * atoms) + 1);
+    return int(most);
+}
 
 // Cycles per MMA of one CTA (pair) for a tile width, fitted to B200 measurements for each
 // variant: the tensor pipe needs bn/2 cycles, but the single issuing thread, the per-stage
@@ -183,7 +208,7 @@ double cycles_per_mma(const Variant &v, int bn) {
 // tiles that would form a partial last wave), is cut into `splits` K ranges whose fp32
 // partials the last arriving split sums. Split units run first; in the hybrid form the whole
 // tiles that follow hide that fix-up, in the plain form it ends the launch.
-double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots, int splits, bool hybrid) {
+double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots, int splits, bool hybrid, int sk = 0) {
     const int64_t tiles = tiles_for(p, v, bn);
     const int64_t atoms = (p->k + gg::kBK - 1) / gg::kBK;
     const double per_mma = cycles_per_mma(v, bn);
@@ -191,7 +216,16 @@ double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots, in
     // matters for launches of a few microseconds.
     double fixed = v.cg == 2 ? 1500.0 : 0.0;
     double unit_atoms;
-    if (splits <= 1) {
+    if (sk > 0) {
+        // stream-K: whole waves, then an equal share of the stream-K region's atoms. Every cluster
+        // writes an fp32 partial and reads one back at about the same time, so the fix-up runs at
+        // the GPU-wide store rate: timestamps inside the kernel show ~3.5-5 us per 128 x 240 fp32
+        // partial per CTA (~16 bytes per cycle per SM) plus ~2 us of fence and arrival latency.
+        const int64_t skt = sk_tiles_for(tiles, slots, atoms, sk);
+        const int64_t S = skt * atoms;
+        unit_atoms = double((tiles - skt) / slots) * double(atoms) + double((S + slots - 1) / slots);
+        fixed += 4000.0 + double(sk_max_pieces(skt, slots, atoms) - 1) * double(bn) * 64.0;
+    } else if (splits <= 1) {
         unit_atoms = double((tiles + slots - 1) / slots) * double(atoms);
     } else {
         const int64_t whole = hybrid ? tiles / slots * slots : 0;
@@ -205,13 +239,15 @@ double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots, in
     return unit_atoms * 4.0 * per_mma + fixed;
 }
 
-// Pick the variant, tile width and split-K form with the smallest modelled time.
+// Pick the variant, tile width and split-K / stream-K form with the smallest modelled time.
 // `forced_variant` >= 0 and `forced_bn` > 0 restrict the search; `min_splits`..`max_splits` is
-// the range of split counts tried; `forced_hybrid` is -1 (either form), 0 or 1. `pairs` is the
-// number of co-resident CTA pairs of the 2-CTA variant.
+// the range of split counts tried; `forced_hybrid` is -1 (either form), 0 or 1; `stream_k` is -1
+// (automatic), 0 (never) or the stream-K kind to use. `pairs` is the number of co-resident CTA
+// pairs of the 2-CTA variant.
 Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_variant, int forced_bn,
-                     int max_splits = 1, bool mn_major_b = false, int min_splits = 1, int forced_hybrid = -1) {
-    Choice best{-1, 0, 1, false};
+                     int max_splits = 1, bool mn_major_b = false, int min_splits = 1, int forced_hybrid = -1,
+                     int stream_k = 0) {
+    Choice best{-1, 0, 1, false, 0};
     double best_t = 0;
     const int64_t atoms = (p->k + gg::kBK - 1) / gg::kBK;
     for (int vi = 0; vi < 3; ++vi) {
@@ -221,14 +257,38 @@ Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_var
         const int slots = v.cg == 2 ? pairs : num_sms;
         if (slots < 1)
             continue;
-        for (int bn = v.bn; bn >= 32; bn -= 32) {
+        for (int bn = v.bn; bn >= 16; bn -= 16) {
             if (forced_bn > 0 && bn != forced_bn)
                 continue;
             if (forced_bn <= 0 && bn < 128)
                 continue;  // narrower tiles are issue-bound; only on request
+            // A width in steps of 16 (not 32) only where it tiles N exactly (N = 2880 = 12 x 240
+            // against 256's 6.7% padding: +2-9% measured); with a ragged N tail it measured
+            // between -5% and +3% against the widths in steps of 32.
+            if (forced_bn <= 0 && bn % 32 != 0 && p->n % bn != 0)
+                continue;
             if (mn_major_b && (bn / v.cg) % 64 != 0)
                 continue;  // MN-major B is loaded in 64-column boxes
             const int64_t tiles = tiles_for(p, v, bn);
+            // stream-K candidates (kinds 1 and 2), unless split-K is forced
+            for (int kind = 1; kind <= 2 && min_splits == 1 && stream_k != 0; ++kind) {
+                if (stream_k > 0 && kind != stream_k)
+                    continue;
+                const int64_t skt = sk_tiles_for(tiles, slots, atoms, kind);
+                if (skt == 0)
+                    continue;
+                const int pieces = sk_max_pieces(skt, slots, atoms);
+                // automatic: at most 4 pieces per tile and >= 4 atoms per cluster
+                if (stream_k < 0 && (pieces > 4 || skt * atoms < 4 * int64_t(slots)))
+                    continue;
+                const double t = model_cycles(p, v, bn, slots, 1, false, kind);
+                if (best.variant < 0 || t < best_t * 0.999) {
+                    best = {vi, bn, pieces, false, kind};
+                    best_t = t;
+                }
+            }
+            if (stream_k > 0)
+                continue;  // a forced stream-K kind is the only form tried
             for (int s = min_splits; s <= max_splits; ++s) {
                 for (int hy = 0; hy < 2; ++hy) {
                     if ((s == 1 && hy == 1) || (forced_hybrid >= 0 && s > 1 && hy != forced_hybrid))
@@ -246,7 +306,7 @@ Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_var
                         continue;  // no partial wave to split
                     const double t = model_cycles(p, v, bn, slots, s, hy == 1);
                     if (best.variant < 0 || t < best_t * 0.999) {
-                        best = {vi, bn, s, hy == 1};
+                        best = {vi, bn, s, hy == 1, 0};
                         best_t = t;
                     }
                 }
@@ -295,9 +355,13 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < -1 || value > 1)
             return fail(h, GG_ERR_ARG, "split_tail must be -1 (auto), 0 (split every tile) or 1 (only the last wave)");
         h->opt_sk_tail = int(value);
+    } else if (!std::strcmp(key, "stream_k")) {
+        if (value < -1 || value > 2)
+            return fail(h, GG_ERR_ARG, "stream_k must be -1 (auto), 0 (off), 1 (partial last wave) or 2 (+ one wave)");
+        h->opt_stream_k = int(value);
     } else if (!std::strcmp(key, "bn")) {
-        if (value != 0 && (value < 32 || value > 256 || value % 32 != 0))
-            return fail(h, GG_ERR_ARG, "bn must be 0 (auto) or a multiple of 32 in 32..256");
+        if (value != 0 && (value < 16 || value > 256 || value % 16 != 0))
+            return fail(h, GG_ERR_ARG, "bn must be 0 (auto) or a multiple of 16 in 16..256");
         h->opt_bn = int(value);
     } else if (!std::strcmp(key, "max_ctas")) {
         if (value < 0)
@@ -458,6 +522,10 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
         return refuse(h, why, why_len, "group_num * n must be below 2^31 for wgrad");
     if (op == gg::kOpWgrad && h->opt_split > 1)
         return refuse(h, why, why_len, "split-K is not available for wgrad (per-group reduction lengths)");
+    if (op == gg::kOpWgrad && h->opt_stream_k > 0)
+        return refuse(h, why, why_len, "stream-K is not available for wgrad (per-group reduction lengths)");
+    if (h->opt_split > 1 && h->opt_stream_k > 0)
+        return refuse(h, why, why_len, "split > 1 and stream_k > 0 exclude each other");
 
     // The problem as the cost model sees it: rows per group, output columns, reduction length.
     const int G = q.group_num;
@@ -519,11 +587,16 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     if (h->opt_split > 1 && h->opt_split > (cm.k + gg::kBK - 1) / gg::kBK)
         return refuse(h, why, why_len, "split exceeds the number of 64-wide K atoms");
     // a forced split count is used exactly (the tiling is chosen for it)
+    // stream-K is tried unless split-K is forced (or for wgrad)
+    const int stream_k = op == gg::kOpWgrad || h->opt_split > 1 ? 0 : h->opt_stream_k;
     const Choice ch = choose_tiling(&cm, num_sms, pairs, h->opt_variant, h->opt_bn, max_splits, mn_b,
-                                    h->opt_split > 1 && op != gg::kOpWgrad ? h->opt_split : 1, h->opt_sk_tail);
+                                    h->opt_split > 1 && op != gg::kOpWgrad ? h->opt_split : 1, h->opt_sk_tail,
+                                    stream_k);
     if (ch.variant < 0)
         return refuse(h, why, why_len,
                       mn_b && h->opt_bn > 0    ? "bn must be a multiple of 64 per CTA for a backward operation"
+                      : stream_k > 0        ? "stream_k: this tiling has no partial last wave (or too few tiles) to "
+                                              "spread"
                       : h->opt_sk_tail == 1 ? "split_tail=1: this tiling has no partial last wave to split"
                                             : "no kernel variant fits this device and these options");
     const int vi = ch.variant;
@@ -547,9 +620,13 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     meta[2 * G + 1] = int32_t(rows);
     // Split-K form: every tile split, or (hybrid) only as many tiles as would form a partial last
     // wave; the split tiles' units run first, the whole tiles after them.
+    // Stream-K instead: the first sk_tiles tiles' atoms dealt out evenly to every cluster.
     const int64_t clusters = std::max(1, v.cg == 2 ? pairs : num_sms);
-    const int64_t split_tiles = ch.splits > 1 ? (ch.hybrid ? tiles % clusters : tiles) : 0;
-    const int64_t units = tiles + split_tiles * (ch.splits - 1);
+    const int64_t atoms = (cm.k + gg::kBK - 1) / gg::kBK;
+    const int64_t sk_tiles = ch.sk > 0 ? sk_tiles_for(tiles, clusters, atoms, ch.sk) : 0;
+    const bool partials = ch.splits > 1 || sk_tiles > 0;  // fp32 workspace + arrival counters
+    const int64_t split_tiles = sk_tiles > 0 ? sk_tiles : ch.splits > 1 ? (ch.hybrid ? tiles % clusters : tiles) : 0;
+    const int64_t units = sk_tiles > 0 ? clusters : tiles + split_tiles * (ch.splits - 1);
 
     if (h->meta_cap < meta.size()) {
         if (h->d_meta)
@@ -562,9 +639,11 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     if (!h->d_status)
         GG_CUDA(h, cudaMalloc(&h->d_status, 16));
     GG_CUDA(h, cudaMemsetAsync(h->d_status, 0, 16, stream));
-    if (ch.splits > 1) {
-        // tile-private partials: per split tile and CTA, 128 rows x bn fp32 per split
-        const size_t ws_bytes = size_t(split_tiles) * size_t(v.cg) * size_t(ch.splits) * 128 * size_t(bn) * sizeof(float);
+    if (partials) {
+        // tile-private partials: per split tile and CTA, 128 rows x bn fp32 (rounded up to whole
+        // 32-column chunks) per split / piece
+        const size_t ws_bytes = size_t(split_tiles) * size_t(v.cg) * size_t(ch.splits) * 128 *
+                                size_t((bn + 31) / 32 * 32) * sizeof(float);
         const size_t ctr_bytes = size_t(split_tiles) * size_t(v.cg) * 4 * sizeof(int32_t);
         if (h->ws_cap < ws_bytes) {
             if (h->d_ws)
@@ -671,9 +750,10 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     kp.bn = bn;
     kp.total_tiles = int32_t(tiles);
     kp.splits = ch.splits;
-    kp.split_tiles = int32_t(split_tiles);
-    kp.ws = ch.splits > 1 ? h->d_ws : nullptr;
-    kp.counters = ch.splits > 1 ? h->d_counters : nullptr;
+    kp.split_tiles = sk_tiles > 0 ? 0 : int32_t(split_tiles);
+    kp.sk_tiles = int32_t(sk_tiles);
+    kp.ws = partials ? h->d_ws : nullptr;
+    kp.counters = partials ? h->d_counters : nullptr;
     kp.band = band;
     kp.raster = raster;
     // epilogue store path: direct stores for tiles with >= 16 K atoms (1024 of reduction)
@@ -691,12 +771,16 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     h->fn = fn;
     h->smem = v.smem;
     h->cg = v.cg;
+    char form[64];
+    if (sk_tiles > 0)
+        std::snprintf(form, sizeof(form), "split=1 stream_k=%lld tiles(<=%d pieces)", (long long)sk_tiles, ch.splits);
+    else
+        std::snprintf(form, sizeof(form), "split=%d%s", ch.splits,
+                      split_tiles > 0 && split_tiles < tiles ? "(last wave)" : "");
     char d[256];
-    std::snprintf(d, sizeof(d),
-                  "gg_sm100<%s%s%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld split=%d%s grid=%d band=%d%s",
+    std::snprintf(d, sizeof(d), "gg_sm100<%s%s%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld %s grid=%d band=%d%s",
                   q.dtype == GG_BF16 ? "bf16" : "fp16", op == gg::kOpForward ? "" : ",", op == gg::kOpForward ? "" : op_name(op),
-                  v.cluster_m, bn, gg::kBK * v.atoms, v.cg, v.stages, (long long)tiles, ch.splits,
-                  split_tiles > 0 && split_tiles < tiles ? "(last wave)" : "", h->grid, band,
+                  v.cluster_m, bn, gg::kBK * v.atoms, v.cg, v.stages, (long long)tiles, form, h->grid, band,
                   raster ? "n" : "");
     h->detail = d;
     h->ready = true;

@@ -12,8 +12,9 @@
 //
 //   * one CTA per SM (kCG = 1) or one CTA pair per two SMs (kCG = 2, tcgen05 cta_group::2),
 //     persistent over a static schedule of work units that covers every group (the scheduler
-//     is on the device: a unit is a tile or a K split of one, a tile index is mapped to
-//     (group, m-tile, n-tile) from per-group tile offsets);
+//     is on the device: a unit is a tile or a contiguous K range of one -- a split-K split or a
+//     stream-K piece --, a tile index is mapped to (group, m-tile, n-tile) from per-group tile
+//     offsets);
 //   * warp 0: TMA producer. 128-byte-swizzled A (128 x 64) and B (BN/kCG x 64) tiles into a
 //     STAGES-deep shared-memory ring guarded by full/empty mbarriers (no multicast: every CTA
 //     loads its own halves);
@@ -98,10 +99,14 @@ struct KernelParams {
     int32_t tiles_n;      // ceil(N / bn)
     int32_t bn;           // tile N of this launch: a multiple of 32, <= the variant's kBN
     int32_t total_tiles;  // tile_off[G]
-    int32_t splits;       // K splits of each split tile (0 or 1 = none)
+    int32_t splits;       // K splits of each split tile (0 or 1 = none); with stream-K the most
+                          // pieces any stream-K tile has (the workspace stride)
     int32_t split_tiles;  // splits > 1: tiles [0, split_tiles) are split in `splits`, the rest run whole
-    float *ws;            // splits > 1: fp32 partial sums, per split tile [kCG][4 warps][splits][bn/32] 4-KB blocks
-    int32_t *counters;    // splits > 1: [split tiles][kCG][4] arrival counts, 0 between launches
+    int32_t sk_tiles;     // > 0: stream-K. The K atoms of tiles [0, sk_tiles) are dealt out in equal
+                          // contiguous ranges to all clusters; the remaining tiles run whole
+    float *ws;            // split / stream-K: fp32 partial sums, per split tile
+                          // [kCG][4 warps][splits][ceil(bn/32)] 4-KB blocks
+    int32_t *counters;    // split / stream-K: [split tiles][kCG][4] arrival counts, 0 between launches
     int32_t band;         // tiles per raster band (L2 reuse, see decode_tile)
     int32_t raster;       // 0: bands of `band` m-tiles, n-tiles swept; 1: bands of `band` n-tiles
     int32_t store_min_atoms;  // a tile with at least this many K atoms stores out straight from
@@ -201,23 +206,73 @@ __device__ __forceinline__ TileCoord decode_tile(const KernelParams &p, int t, i
     return tc;
 }
 
-// A work unit: a whole tile, or one K split of a split tile. Units [0, split_tiles x splits) are
-// the splits of tiles [0, split_tiles), scheduled first so that the split-K fix-up (partials
-// written, the last arriver's reduction) runs in the epilogue warps while the MMA warp works on
-// the whole tiles that follow; then one unit per remaining tile. split_tiles = total_tiles is
-// plain split-K; fewer split tiles is split-K for what would otherwise be a partial last wave.
+// A work unit: K atoms [atom0, atom1) of tile t, piece `piece` of the `npieces` pieces the tile
+// is cut into (npieces > 1: every piece publishes an fp32 partial and the last to arrive sums them
+// in piece order). Each cluster (CTA or CTA pair) walks its own list of units, in order:
+//   split-K (splits > 1, sk_tiles == 0): units [0, split_tiles x splits) are the equal K splits of
+//     tiles [0, split_tiles), then one unit per remaining tile; unit u goes to cluster
+//     u % clusters. split_tiles = total_tiles is plain split-K; fewer split tiles is split-K for
+//     what would otherwise be a partial last wave.
+//   stream-K (sk_tiles > 0): the sk_tiles x num_kb atoms of tiles [0, sk_tiles), in tile-major
+//     order, are cut into one contiguous range per cluster (cluster c: [c S / C, (c+1) S / C),
+//     S atoms, C clusters), split at tile boundaries into pieces; then whole tiles
+//     sk_tiles + c, sk_tiles + c + C, ... Every cluster gets the same number of atoms (+-1),
+//     whatever the number of tiles.
+// Either way the pieces of a tile come first in each cluster's list, so the fix-up runs in the
+// epilogue warps while the MMA warp works on what follows.
 struct Unit {
-    int t, split, nsplit;
+    int t, atom0, atom1, piece, npieces;
 };
-__device__ __forceinline__ Unit unit_of(const KernelParams &p, int u) {
-    const int s = p.splits > 1 ? p.splits : 1;
-    if (s == 1)
-        return {u, 0, 1};
-    if (u < p.split_tiles * s) {
-        const int q = u / s;
-        return {q, u - q * s, s};
+
+// Stream-K: the cluster whose range holds atom g (S = atoms in the stream-K region; S >= C).
+__device__ __forceinline__ int sk_cluster_of(int64_t g, int64_t S, int C) { return int(((g + 1) * C - 1) / S); }
+
+struct UnitList {
+    int n;              // units of this cluster
+    int n_sk;           // stream-K pieces among them (listed first)
+    int64_t sk0, sk1;   // stream-K: this cluster's atom range
+};
+
+__device__ __forceinline__ UnitList units_of(const KernelParams &p, int c, int C) {
+    UnitList l{0, 0, 0, 0};
+    if (p.sk_tiles > 0) {
+        const int64_t A = p.num_kb, S = int64_t(p.sk_tiles) * A;
+        l.sk0 = S * c / C;
+        l.sk1 = S * (c + 1) / C;
+        l.n_sk = l.sk1 > l.sk0 ? int((l.sk1 - 1) / A - l.sk0 / A + 1) : 0;
+        const int rest = p.total_tiles - p.sk_tiles - c;
+        l.n = l.n_sk + (rest > 0 ? (rest + C - 1) / C : 0);
+    } else {
+        const int s = p.splits > 1 ? p.splits : 1;
+        const int total = p.total_tiles + (s > 1 ? p.split_tiles * (s - 1) : 0);
+        l.n = c < total ? (total - c + C - 1) / C : 0;
     }
-    return {u - p.split_tiles * (s - 1), 0, 1};
+    return l;
+}
+
+__device__ __forceinline__ Unit unit_at(const KernelParams &p, const UnitList &l, int c, int C, int i) {
+    const int A = p.num_kb;
+    if (p.sk_tiles > 0) {
+        if (i < l.n_sk) {
+            const int64_t S = int64_t(p.sk_tiles) * A;
+            const int t = int(l.sk0 / A) + i;
+            const int64_t t0 = int64_t(t) * A;
+            const int first = sk_cluster_of(t0, S, C);
+            const int last = sk_cluster_of(t0 + A - 1, S, C);
+            return {t, int((l.sk0 > t0 ? l.sk0 : t0) - t0), int((l.sk1 < t0 + A ? l.sk1 : t0 + A) - t0), c - first,
+                    last - first + 1};
+        }
+        return {p.sk_tiles + c + (i - l.n_sk) * C, 0, A, 0, 1};
+    }
+    const int u = c + i * C;
+    const int s = p.splits > 1 ? p.splits : 1;
+    if (s > 1 && u < p.split_tiles * s) {
+        // split j of s covers atoms [j A / s, (j + 1) A / s): balanced, never empty while s <= A
+        const int q = u / s;
+        const int j = u - q * s;
+        return {q, j * A / s, (j + 1) * A / s, j, s};
+    }
+    return {s > 1 ? u - p.split_tiles * (s - 1) : u, 0, A, 0, 1};
 }
 
 struct Abort {
@@ -254,6 +309,28 @@ __device__ __forceinline__ bool wait_one(uint32_t bar, uint32_t parity, const Ab
     if (kClusterScope ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity))
         return true;
     return wait_slow<kClusterScope>(bar, parity, ab, code);
+}
+
+// Bounded wait by one thread until a global counter, written by other CTAs, reaches `want`.
+// Returns false if this or another role gave up.
+__device__ __noinline__ bool wait_count(const int32_t *ctr, int want, const Abort ab, uint32_t code) {
+    const uint64_t t0 = ptx::globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (*reinterpret_cast<const volatile int32_t *>(ctr) >= want)
+            return true;
+        __nanosleep(32);
+        if ((it & 63u) == 0) {
+            if (*ab.flag != 0u || *(volatile uint32_t *)ab.status != 0u) {
+                *ab.flag = 1u;
+                return false;
+            }
+            if (ptx::globaltimer() - t0 > ab.timeout_ns) {
+                atomicCAS(ab.status, 0u, code);
+                *ab.flag = 1u;
+                return false;
+            }
+        }
+    }
 }
 
 // Warp-uniform bounded wait: lane 0 waits, the result is broadcast.
@@ -365,9 +442,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // reaches this launch (prepare synchronises its stream), never by a preceding kernel, so the
     // first tile's look-up may also run before the dependency wait, bringing the table's first
     // lines into this SM's cache meanwhile. Every other global access comes after the wait.
-    if (threadIdx.x == 0) {
+    const UnitList units = units_of(p, cluster_id, num_clusters);
+    if (threadIdx.x == 0 && units.n > 0) {
         int cur = 0;
-        const TileCoord tc0 = decode_tile<C::kClusterM, kOp>(p, unit_of(p, cluster_id).t, cur);
+        const TileCoord tc0 = decode_tile<C::kClusterM, kOp>(p, unit_at(p, units, cluster_id, num_clusters, 0).t, cur);
         tmem_ptr_slot[2] = uint32_t(tc0.g + tc0.rows);  // keeps the loads (slot otherwise unused)
     }
     ptx::griddep_wait();
@@ -378,13 +456,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::griddep_launch_dependents();
 
     const Abort ab{p.status, abort_flag, p.timeout_ns};
-    // Work units (unit_of): the K splits of the split tiles, then the whole tiles. A split covers a
-    // contiguous range of K atoms; each unit runs the same producer/MMA/epilogue pipeline over its
-    // range. (wgrad runs unsplit: its reduction length differs per group.)
-    const int splits = p.splits > 1 ? p.splits : 1;
-    const int total_units = p.total_tiles + p.split_tiles * (splits - 1);
-    // Split i of n covers K atoms [i * num_kb / n, (i + 1) * num_kb / n): balanced, and never empty
-    // while n <= num_kb (the host refuses more splits than atoms).
+    // Work units (unit_at): each covers a contiguous range of K atoms of one tile and runs the same
+    // producer/MMA/epilogue pipeline over it. (wgrad runs whole tiles: its reduction length differs
+    // per group.)
 
     if (warp == 0) {
         // ---------------- TMA producer (one thread) ----------------
@@ -395,11 +469,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t ph = 0;
             bool ok = true;
             int fenced_g = -1;  // wgrad: group whose tensor maps this thread has acquired
-            for (int u = cluster_id; u < total_units && ok; u += num_clusters) {
-                const Unit un = unit_of(p, u);
+            for (int i = 0; i < units.n && ok; ++i) {
+                const Unit un = unit_at(p, units, cluster_id, num_clusters, i);
                 const TileCoord tc = decode_tile<C::kClusterM, kOp>(p, un.t, cursor);
-                const int atom0 = kOp == kOpWgrad ? 0 : un.split * p.num_kb / un.nsplit;
-                const int atom1 = kOp == kOpWgrad ? tc.red_atoms : (un.split + 1) * p.num_kb / un.nsplit;
+                const int atom0 = kOp == kOpWgrad ? 0 : un.atom0;
+                const int atom1 = kOp == kOpWgrad ? tc.red_atoms : un.atom1;
                 const int num_ks = (atom1 - atom0 + kAtoms - 1) / kAtoms;
                 // A: first row (forward/dgrad: token row; wgrad: row of dw[g], a column of dy)
                 const int a_row = (kOp == kOpWgrad ? 0 : tc.out_row0) + tc.mt * C::kClusterM + int(cta_rank) * kBM;
@@ -427,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t b_dst = a_dst + C::kABytes;
                     const uint32_t fb = full_leader0 + 8u * s;
                     // test hook: the leader skips its arrive and loads of cluster 0's first stage
-                    const bool skip = p.test_stall != 0 && cluster_id == 0 && leader && ks == 0 && u == cluster_id;
+                    const bool skip = p.test_stall != 0 && cluster_id == 0 && leader && ks == 0 && i == 0;
                     if (leader && !skip)
                         ptx::mbar_arrive_expect_tx(full_bar(s), uint32_t(kCG * na * (C::kAAtomBytes + b_rows * kBK * 2)));
 #pragma unroll
@@ -479,15 +553,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t ph = 0;
             bool ok = true;
             int cursor = 0;
-            for (int u = cluster_id; u < total_units && ok; u += num_clusters, ++tl) {
-                int atom0, atom1;
+            for (int i = 0; i < units.n && ok; ++i, ++tl) {
+                const Unit un = unit_at(p, units, cluster_id, num_clusters, i);
+                int atom0 = un.atom0, atom1 = un.atom1;
                 if constexpr (kOp == kOpWgrad) {
                     atom0 = 0;
-                    atom1 = decode_tile<C::kClusterM, kOp>(p, u, cursor).red_atoms;  // 0 for an empty group
-                } else {
-                    const Unit un = unit_of(p, u);
-                    atom0 = un.split * p.num_kb / un.nsplit;
-                    atom1 = (un.split + 1) * p.num_kb / un.nsplit;
+                    atom1 = decode_tile<C::kClusterM, kOp>(p, un.t, cursor).red_atoms;  // 0 for an empty group
                 }
                 const int num_ks = (atom1 - atom0 + kAtoms - 1) / kAtoms;
                 const int acc = int(tl & 1u);
@@ -558,11 +629,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         int out_buf = 0;
         int cursor = 0;
         uint32_t tl = 0;
-        for (int u = cluster_id; u < total_units; u += num_clusters, ++tl) {
-            const Unit un = unit_of(p, u);
+        for (int i = 0; i < units.n; ++i, ++tl) {
+            const Unit un = unit_at(p, units, cluster_id, num_clusters, i);
             const int t = un.t;
-            const int split = un.split;
-            const int nsplit = un.nsplit;
+            const int split = un.piece;
+            const int nsplit = un.npieces;
             const TileCoord tc = decode_tile<C::kClusterM, kOp>(p, t, cursor);
             const int acc = int(tl & 1u);
             const uint32_t acc_ph = (tl >> 1) & 1u;
@@ -579,35 +650,49 @@ __global__ void __launch_bounds__(kThreads, 1)
             T *orow = out + grow * p.n;
             const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * kBN);
             bool store_out = true;
-            const int nch = bn / 32;  // 32-column chunks of the tile
-            // split-K: first float4 of this warp's workspace region (nsplit x nch blocks of 4 KB)
-            const int64_t ws_warp = ((int64_t(t) * kCG + int(cta_rank)) * 4 + q) * int64_t(nsplit) * nch * 256;
+            // 32-column chunks of the tile (a tile width of 16 mod 32 ends in a half chunk: it is read
+            // whole from TMEM, inside the accumulator buffer, and its upper 16 columns are dropped)
+            const int nch = (bn + 31) / 32;
+            // split-K: first float4 of this warp's workspace region (p.splits x nch blocks of 4 KB)
+            const int64_t ws_warp = ((int64_t(t) * kCG + int(cta_rank)) * 4 + q) * int64_t(p.splits) * nch * 256;
             if (nsplit > 1) {
-                // Split-K: publish this unit's fp32 partial; the last of the tile's splits to
-                // arrive (per CTA and warp) sums all of them in split order and stores out.
-                // This warp's workspace blocks of the tile: [split][chunk], each block the 32 x 32
+                // A tile in pieces. Each piece but the one that sums publishes its fp32 partial and
+                // counts itself in (per tile, CTA and warp). Split-K: the splits of a tile run side
+                // by side, so whichever arrives last sums them. Stream-K: piece 0 is the end of its
+                // cluster's range, processed after the other pieces (the starts of theirs), so it
+                // is the fixed summer: it writes no partial and waits (bounded) for the others'.
+                // This warp's workspace blocks of the tile: [piece][chunk], each block the 32 x 32
                 // fp32 fragment of one tcgen05.ld in lane order (float4 j of lane l at j * 32 + l),
                 // so every warp access is 512 contiguous bytes.
-                float4 *wsw = reinterpret_cast<float4 *>(p.ws) + ws_warp + (int64_t(split) * nch) * 256 + lane;
-#pragma unroll 1
-                for (int c = 0; c < nch; ++c) {
-                    uint32_t r[32];
-                    ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
-                    ptx::tmem_wait_ld(r);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        __stcg(wsw + c * 256 + j * 32,
-                               make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                           __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
-                }
-                __threadfence();
-                __syncwarp();
                 int32_t *ctr = p.counters + (int64_t(t) * kCG + int(cta_rank)) * 4 + q;
-                int prev = 0;
-                if (lane == 0)
-                    prev = atomicAdd(ctr, 1);
-                prev = __shfl_sync(0xffffffffu, prev, 0);
-                store_out = prev == nsplit - 1;
+                const bool fixed_summer = p.sk_tiles > 0 && split == 0;
+                if (!fixed_summer) {
+                    float4 *wsw = reinterpret_cast<float4 *>(p.ws) + ws_warp + (int64_t(split) * nch) * 256 + lane;
+#pragma unroll 1
+                    for (int c = 0; c < nch; ++c) {
+                        uint32_t r[32];
+                        ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
+                        ptx::tmem_wait_ld(r);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            __stcg(wsw + c * 256 + j * 32,
+                                   make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+                    }
+                    __threadfence();
+                    __syncwarp();
+                    int prev = 0;
+                    if (lane == 0)
+                        prev = atomicAdd(ctr, 1);
+                    prev = __shfl_sync(0xffffffffu, prev, 0);
+                    store_out = p.sk_tiles == 0 && prev == nsplit - 1;
+                } else {
+                    int ok = 1;
+                    if (lane == 0)
+                        ok = wait_count(ctr, nsplit - 1, ab, kStatusTimeout | kRoleEpilogue | 0x30u | uint32_t(q)) ? 1 : 0;
+                    if (__shfl_sync(0xffffffffu, ok, 0) == 0)
+                        break;
+                }
                 if (store_out) {
                     __threadfence();
                     if (lane == 0)
@@ -660,91 +745,113 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 out_buf ^= 1;
             }
-            // Split-K reduction by the last arriver: the other splits' blocks are read in (chunk,
-            // split) order with one block always in flight ahead of the one being added.
-            const int others = nsplit - 1;
-            auto other_blk = [&](int idx) {
-                const int c = idx / others;
-                const int o = idx - c * others;
-                const int s2 = o + (o >= split ? 1 : 0);
-                return reinterpret_cast<const float4 *>(p.ws) + ws_warp + (int64_t(s2) * nch + c) * 256 + lane;
-            };
-            float4 nxt[8];
-            int blk = 0;
-            if (store_out && nsplit > 1) {
-                const float4 *src = other_blk(0);
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    nxt[j] = __ldcg(src + j * 32);
-            }
-#pragma unroll 1
-            for (int c = c_tma; store_out && c < bn / 32; ++c) {
-                uint32_t r[32];
-                ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
-                ptx::tmem_wait_ld(r);
-                if (zero_tile) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        r[j] = 0u;
-                }
+            const int col_end = min(p.n, tc.nt * bn + bn);  // tile's last column + 1
+            // Store 32 accumulator columns (fp32 bits) of this lane's row: whole 32-byte sectors
+            // where the row allows (N % 16 == 0 keeps rows 32-byte aligned), else 16-byte pieces;
+            // columns past the tile or past N are skipped in 8s.
+            auto store_chunk = [&](int c, const uint32_t (&r)[32]) {
+                if (!row_ok)
+                    return;
                 const int col = tc.nt * bn + c * 32;
-                if (nsplit > 1) {
-                    // r = sum over splits 0..nsplit-1 in that order; this unit's own part from TMEM
-                    float sum[32];
+                uint32_t h[16];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        sum[j] = 0.f;
-                    for (int s2 = 0; s2 < nsplit; ++s2) {
-                        if (s2 == split) {
+                for (int j = 0; j < 16; ++j)
+                    h[j] = pack2<T>(r[2 * j], r[2 * j + 1]);
 #pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                sum[j] += __uint_as_float(r[j]);
-                        } else {
-                            float4 cur[8];
+                for (int hh = 0; hh < 2; ++hh) {
+                    T *dst = orow + col + hh * 16;
+                    if (col + hh * 16 + 16 <= col_end && (reinterpret_cast<uintptr_t>(dst) & 31u) == 0) {
+                        ptx::st_cs_v8(dst, h[8 * hh], h[8 * hh + 1], h[8 * hh + 2], h[8 * hh + 3], h[8 * hh + 4],
+                                      h[8 * hh + 5], h[8 * hh + 6], h[8 * hh + 7]);
+                    } else {
 #pragma unroll
-                            for (int j = 0; j < 8; ++j)
-                                cur[j] = nxt[j];
-                            if (++blk < nch * others) {
-                                const float4 *src = other_blk(blk);
+                        for (int j = 0; j < 2; ++j)
+                            if (col + hh * 16 + j * 8 < col_end)
+                                __stcs(reinterpret_cast<uint4 *>(dst + j * 8),
+                                       make_uint4(h[8 * hh + 4 * j], h[8 * hh + 4 * j + 1], h[8 * hh + 4 * j + 2],
+                                                  h[8 * hh + 4 * j + 3]));
+                    }
+                }
+            };
+            if (store_out && nsplit > 1) {
+                // Sum of the tile's pieces 0..nsplit-1 in that order (this unit's own from TMEM),
+                // chunk by chunk. The other pieces' blocks stream in (chunk, piece) order through a
+                // ring of kPrefetch register buffers, so that many L2 reads are in flight at once;
+                // the ring is indexed at compile time (block b sits in buffer b % kPrefetch).
+                constexpr int kPrefetch = 3;
+                const int others = nsplit - 1;
+                const int nb = nch * others;
+                auto load_blk = [&](int b, float4 (&dst)[8]) {
+                    const int c = b / others;
+                    const int o = b - c * others;
+                    const int s2 = o + (o >= split ? 1 : 0);
+                    const float4 *src = reinterpret_cast<const float4 *>(p.ws) + ws_warp + (int64_t(s2) * nch + c) * 256 + lane;
 #pragma unroll
-                                for (int j = 0; j < 8; ++j)
-                                    nxt[j] = __ldcg(src + j * 32);
+                    for (int j = 0; j < 8; ++j)
+                        dst[j] = __ldcg(src + j * 32);
+                };
+                float4 pf[kPrefetch][8];
+#pragma unroll
+                for (int i = 0; i < kPrefetch; ++i)
+                    if (i < nb)
+                        load_blk(i, pf[i]);
+                uint32_t r[32];
+                float sum[32];
+#pragma unroll 1
+                for (int b0 = 0; b0 < nb; b0 += kPrefetch) {
+#pragma unroll
+                    for (int i = 0; i < kPrefetch; ++i) {
+                        const int b = b0 + i;
+                        if (b < nb) {
+                            const int c = b / others;
+                            const int o = b - c * others;
+                            if (o == 0) {
+                                ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
+                                ptx::tmem_wait_ld(r);
+#pragma unroll
+                                for (int j = 0; j < 32; ++j)
+                                    sum[j] = 0.f;
+                            }
+                            if (o == split) {
+#pragma unroll
+                                for (int j = 0; j < 32; ++j)
+                                    sum[j] += __uint_as_float(r[j]);
                             }
 #pragma unroll
                             for (int j = 0; j < 8; ++j) {
-                                sum[4 * j] += cur[j].x;
-                                sum[4 * j + 1] += cur[j].y;
-                                sum[4 * j + 2] += cur[j].z;
-                                sum[4 * j + 3] += cur[j].w;
+                                sum[4 * j] += pf[i][j].x;
+                                sum[4 * j + 1] += pf[i][j].y;
+                                sum[4 * j + 2] += pf[i][j].z;
+                                sum[4 * j + 3] += pf[i][j].w;
+                            }
+                            if (b + kPrefetch < nb)
+                                load_blk(b + kPrefetch, pf[i]);
+                            if (o == others - 1) {
+                                if (split == others) {
+#pragma unroll
+                                    for (int j = 0; j < 32; ++j)
+                                        sum[j] += __uint_as_float(r[j]);
+                                }
+#pragma unroll
+                                for (int j = 0; j < 32; ++j)
+                                    r[j] = __float_as_uint(sum[j]);
+                                store_chunk(c, r);
                             }
                         }
                     }
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        r[j] = __float_as_uint(sum[j]);
                 }
-                if (row_ok) {
-                    uint32_t h[16];
+            } else {
+#pragma unroll 1
+                for (int c = c_tma; store_out && c < nch; ++c) {
+                    uint32_t r[32];
+                    ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
+                    ptx::tmem_wait_ld(r);
+                    if (zero_tile) {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        h[j] = pack2<T>(r[2 * j], r[2 * j + 1]);
-                    // whole 32-byte sectors where the row allows (N % 16 == 0 keeps rows 32-byte
-                    // aligned), else 16-byte pieces; columns past N are skipped in 8s
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        T *dst = orow + col + hh * 16;
-                        if (col + hh * 16 + 16 <= p.n && (reinterpret_cast<uintptr_t>(dst) & 31u) == 0) {
-                            ptx::st_cs_v8(dst, h[8 * hh], h[8 * hh + 1], h[8 * hh + 2], h[8 * hh + 3], h[8 * hh + 4],
-                                          h[8 * hh + 5], h[8 * hh + 6], h[8 * hh + 7]);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 2; ++j)
-                                if (col + hh * 16 + j * 8 < p.n)
-                                    __stcs(reinterpret_cast<uint4 *>(dst + j * 8),
-                                           make_uint4(h[8 * hh + 4 * j], h[8 * hh + 4 * j + 1], h[8 * hh + 4 * j + 2],
-                                                      h[8 * hh + 4 * j + 3]));
-                        }
+                        for (int j = 0; j < 32; ++j)
+                            r[j] = 0u;
                     }
+                    store_chunk(c, r);
                 }
             }
             ptx::tc_fence_before();

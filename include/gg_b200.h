@@ -135,10 +135,15 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
  *   "variant"    -1 auto, 0 = 2-CTA 256x256 tile, 1 = 1-CTA 128x256, 2 = 1-CTA 128x128
  *   "band"       tiles per raster band (default chosen per shape), 0 = auto
  *   "raster"     -1 auto (= 0), 0 = bands of M tiles (weight panels shared), 1 = bands of N tiles
- *   "bn"         tile width (multiple of 32, <= the variant's), 0 = auto (cost model)
+ *   "bn"         tile width (multiple of 16, <= the variant's), 0 = auto (cost model)
  *   "split"      K splits per split tile (split-K with an fp32 workspace), 0 = auto, 1 = none
  *   "split_tail" -1 auto, 0 = split every tile, 1 = split only the tiles of what would be a
  *                partial last wave (their units run first, whole tiles after them)
+ *   "stream_k"   0 (default) = off, -1 = the cost model decides, 1 = stream-K over the tiles of
+ *                what would be a partial last wave, 2 = over those and one full wave more: their
+ *                K atoms are dealt out in equal contiguous ranges to all CTAs (pairs), tiles cut
+ *                at arbitrary atoms are summed through an fp32 workspace (forward and dgrad;
+ *                refused with "split" > 1, for wgrad, and where the tiling has no partial wave)
  *   "store"      -1 auto (direct stores from registers for tiles with >= 16 K atoms, staging +
  *                TMA stores for shorter ones), 0 = always TMA stores, 1 = always direct stores
  *   "pdl"        1 (default) = launch with programmatic stream serialisation, so the launch and

@@ -136,7 +136,7 @@ public:
         return st;
     }
 
-    // Knobs of gg_set_option ("variant", "band", "max_ctas", "timeout_ms").
+    // Knobs of gg_set_option ("variant", "bn", "split", "stream_k", "max_ctas", ...; gg_b200.h).
     void set_option(const char *key, int64_t value) {
         if (gg_set_option(h_, key, value) != GG_OK)
             throw std::invalid_argument(gg_last_error(h_));

@@ -65,10 +65,12 @@ def test_set_option(gg):
     b.set_option("split", 2)
     b.set_option("split", 0)
     for key, val in (("split_tail", -1), ("split_tail", 0), ("split_tail", 1), ("raster", 1), ("raster", -1),
-                     ("pdl", 0), ("pdl", 1), ("store", -1), ("store", 0), ("store", 1)):
+                     ("pdl", 0), ("pdl", 1), ("store", -1), ("store", 0), ("store", 1), ("stream_k", -1),
+                     ("stream_k", 0), ("stream_k", 1), ("stream_k", 2), ("bn", 240), ("bn", 16), ("bn", 0)):
         b.set_option(key, val)
     for key, val in (("variant", 7), ("band", -1), ("timeout_ms", 0), ("test_stall", 2), ("bn", 100), ("bn", 288), ("split", 9),
-                     ("split_tail", 2), ("raster", 2), ("pdl", 3), ("store", 2), ("bogus", 1)):
+                     ("split_tail", 2), ("raster", 2), ("pdl", 3), ("store", 2), ("bogus", 1), ("bn", 24), ("bn", 8),
+                     ("stream_k", 3), ("stream_k", -2)):
         with pytest.raises(gg.GGError):
             b.set_option(key, val)
 
@@ -157,3 +159,14 @@ def test_prepare_grad_rejects_unknown_op_and_wgrad_split(gg):
     b.set_option("split", 2)
     assert "wgrad" in b.prepare_grad(gg.OP_WGRAD, gg.BF16, [4], 64, 64, dy_ptr=ALIGNED, x_ptr=ALIGNED,
                                      dw_ptr=ALIGNED)
+    b.set_option("split", 0)
+    b.set_option("stream_k", 1)
+    assert "stream-K is not available for wgrad" in b.prepare_grad(gg.OP_WGRAD, gg.BF16, [4], 64, 64, dy_ptr=ALIGNED,
+                                                                    x_ptr=ALIGNED, dw_ptr=ALIGNED)
+
+
+def test_split_and_stream_k_exclude_each_other(gg):
+    b = gg.B200Backend()
+    b.set_option("split", 2)
+    b.set_option("stream_k", 2)
+    assert "exclude each other" in b.prepare(gg.BF16, [128], 64, 64, ALIGNED, ALIGNED, ALIGNED)

@@ -3,10 +3,11 @@ against the CPU oracle (the reference's pass rule, bench/bench_main.cpp:264-270)
 
 Each case draws ragged group sizes (some empty), N and K with tails, a dtype, and a random mix
 of the options that change the kernel's schedule: variant, tile width, split count and form
-(every tile or only the last partial wave), raster order and band, and a capped grid (so small
-problems still have several waves). A combination the library refuses must be refused with one
-of its documented reasons; every accepted one must match the oracle exactly within tolerance
-and leave the guard region after the output untouched.
+(every tile or only the last partial wave) or stream-K kind, raster order and band, and a capped
+grid (so small problems still have several waves). A combination the library refuses must be
+refused with one of its documented reasons; every accepted one must match the oracle within
+tolerance, give the same bits on a second run, and leave the guard region after the output
+untouched.
 """
 import numpy as np
 import pytest
@@ -16,7 +17,7 @@ pytestmark = pytest.mark.gpu
 CANARY = 0x7E5A
 GUARD = 2048
 REFUSALS = ("multiple of 64", "split exceeds", "split_tail=1", "split-K is not available", "no kernel variant",
-            "wider than the variant")
+            "wider than the variant", "stream_k: this tiling", "stream-K is not available")
 
 
 def _torch():
@@ -50,11 +51,33 @@ def draw_case(rng):
     return group_m, n, k, op, dtype, opts
 
 
+def draw_case_stream_k(rng):
+    """A case as above with stream-K (automatic, off, or forced to either kind) in place of
+    split-K, tile widths in steps of 16, and a capped grid more often."""
+    group_m, n, k, op, dtype, opts = draw_case(rng)
+    opts.pop("split", None)
+    opts.pop("split_tail", None)
+    if rng.random() < 0.7:
+        opts["bn"] = 16 * int(rng.integers(1, 17))
+    opts["stream_k"] = int(rng.integers(-1, 3))
+    if rng.random() < 0.7:
+        opts["max_ctas"] = int(rng.choice([4, 6, 10, 22, 40]))
+    return group_m, n, k, op, dtype, opts
+
+
 @pytest.mark.parametrize("seed", range(96))
 def test_random_case(gg, orc, seed):
+    check_case(gg, orc, draw_case(np.random.default_rng(1000 + seed)))
+
+
+@pytest.mark.parametrize("seed", range(48))
+def test_random_case_stream_k(gg, orc, seed):
+    check_case(gg, orc, draw_case_stream_k(np.random.default_rng(5000 + seed)))
+
+
+def check_case(gg, orc, drawn):
     torch = _torch()
-    rng = np.random.default_rng(1000 + seed)
-    group_m, n, k, op, dtype, opts = draw_case(rng)
+    group_m, n, k, op, dtype, opts = drawn
     total = sum(group_m)
     s = torch.cuda.current_stream().cuda_stream
     b = gg.B200Backend()
@@ -88,10 +111,15 @@ def test_random_case(gg, orc, seed):
     if why:
         assert any(r in why for r in REFUSALS), (case, why)
         return
+    first_res = None
     for _ in range(2):  # twice: split-K arrival counters must be back at zero
         b.run(s)
         assert b.device_status(s) == 0, (case, b.detail())
         res = out.cpu().numpy().view(np.uint16)
+        if first_res is None:
+            first_res = res.copy()
+        else:  # the same bits again: the partial sums are added in a fixed order
+            assert np.array_equal(first_res, res), (case, b.detail(), "second run differs")
         assert np.all(res[rows * cols:] == CANARY), (case, b.detail(), "store past the end")
         if rows:
             bad, mx, first = orc.check16(res[:rows * cols].reshape(rows, cols), ref, dtype)

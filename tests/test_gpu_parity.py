@@ -270,7 +270,10 @@ def test_config_expert_parallel_shards_equal_whole(gg, orc):
     """BASELINE config E (B=256, M=512, N=4096, K=7168): the full run is checked on the reference
     sample rule against a torch fp32 reference on the GPU (host generation of 17 GB of inputs is
     too slow for a test), and each 8-way expert shard run separately (the per-GPU work of the
-    8-GPU configuration) must reproduce its rows of the full run bit for bit."""
+    8-GPU configuration) must reproduce its rows of the full run bit for bit. Bit equality holds
+    when every tile is accumulated in one pass over K, so both runs are pinned to that form: with
+    stream-K or split-K the tiles cut into pieces depend on the tile count, and a piece boundary
+    changes the fp32 summation order (within tolerance, not bit for bit)."""
     torch = _torch()
     G, M, n, k = 256, 512, 4096, 7168
     gen = torch.Generator(device="cuda").manual_seed(1234)
@@ -278,7 +281,8 @@ def test_config_expert_parallel_shards_equal_whole(gg, orc):
     w = torch.randn(G, n, k, device="cuda", generator=gen).to(torch.bfloat16)
     out = torch.empty(G * M, n, device="cuda", dtype=torch.bfloat16)
     b = gg.B200Backend()
-    b.set_option("variant", 0)
+    for key, val in (("variant", 0), ("split", 1), ("stream_k", 0)):
+        b.set_option(key, val)
     s = torch.cuda.current_stream().cuda_stream
     assert b.prepare(0, [M] * G, n, k, x.data_ptr(), w.data_ptr(), out.data_ptr(), s) == ""
     b.run(s)
@@ -295,7 +299,8 @@ def test_config_expert_parallel_shards_equal_whole(gg, orc):
         g0, g1 = gg.expert_shard(G, 8, r)
         shard = torch.empty((g1 - g0) * M, n, device="cuda", dtype=torch.bfloat16)
         bs = gg.B200Backend()
-        bs.set_option("variant", 0)
+        for key, val in (("variant", 0), ("split", 1), ("stream_k", 0)):
+            bs.set_option(key, val)
         assert bs.prepare(0, [M] * (g1 - g0), n, k, x[g0 * M:].data_ptr(), w[g0].data_ptr(),
                           shard.data_ptr(), s) == ""
         bs.run(s)
@@ -374,3 +379,136 @@ def test_dgrad_split_k_last_wave_only(gg, orc):
     assert b.device_status(s) == 0
     bad, mx, first = orc.check16(dx.cpu().numpy().view(np.uint16).reshape(-1, k), ref, 0)
     assert bad == 0, (b.detail(), bad, mx, first)
+
+
+def _run_opts(gg, torch, group_m, n, k, dtype, xd, wd, opts, runs=2):
+    """Prepare with `opts`, run `runs` times (arrival counters must be back at zero after each),
+    and return (list of output bit arrays, detail)."""
+    total = sum(group_m)
+    out = torch.full((total * n + GUARD,), CANARY, dtype=torch.int16, device="cuda")
+    b = gg.B200Backend()
+    for key, val in opts.items():
+        b.set_option(key, val)
+    s = torch.cuda.current_stream().cuda_stream
+    why = b.prepare(dtype, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s)
+    assert why == "", why
+    results = []
+    for _ in range(runs):
+        out[:total * n].fill_(0)
+        b.run(s)
+        assert b.device_status(s) == 0, b.detail()
+        res = out.cpu().numpy().view(np.uint16)
+        assert np.all(res[total * n:] == CANARY), (b.detail(), "store past the end of out")
+        results.append(res[:total * n].reshape(total, n).copy())
+    return results, b.detail()
+
+
+@pytest.mark.parametrize("variant,bn", [(0, 256), (0, 176), (1, 256), (1, 144), (2, 128), (2, 80)])
+@pytest.mark.parametrize("kind", [1, 2])
+def test_stream_k_forced(gg, orc, variant, bn, kind):
+    """Stream-K: the grid is capped at 10 CTAs; the K atoms of the partial last wave's tiles
+    (kind 1), or of those and one wave more (kind 2), are dealt out evenly to every cluster, so
+    tiles are cut into pieces of different lengths at arbitrary atoms. Two launches in a row
+    reuse the arrival counters; the result is bit-identical both times (fixed summation order)."""
+    torch = _torch()
+    group_m, n, k = [300, 0, 17, 513], 1000, 1000
+    x, w = orc.make_inputs(group_m, n, k, 0)
+    ref = orc.grouped_gemm_f32(x, w, group_m, 0)
+    xd, wd = upload(torch, x), upload(torch, w)
+    res, detail = _run_opts(gg, torch, group_m, n, k, 0, xd, wd,
+                            {"variant": variant, "bn": bn, "stream_k": kind, "max_ctas": 10})
+    assert "stream_k=" in detail, detail
+    for r in res:
+        bad, mx, first = orc.check16(r, ref, 0)
+        assert bad == 0, (detail, bad, mx, first)
+    assert np.array_equal(res[0], res[1]), detail
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_stream_k_fewer_tiles_than_pairs(gg, orc, dtype):
+    """BASELINE config P, B=1 variant (M=1000, N=2880, K=2880): fewer pair tiles than CTA pairs,
+    so stream-K cuts every tile in two or three pieces over the whole GPU. Full-output compare."""
+    torch = _torch()
+    group_m, n, k = [1000], 2880, 2880
+    x, w = orc.make_inputs(group_m, n, k, dtype)
+    ref = orc.grouped_gemm_f32(x, w, group_m, dtype)
+    xd, wd = upload(torch, x), upload(torch, w)
+    for bn in (240, 256):
+        res, detail = _run_opts(gg, torch, group_m, n, k, dtype, xd, wd, {"variant": 0, "bn": bn, "stream_k": 1})
+        assert "stream_k=" in detail, detail
+        for r in res:
+            bad, mx, first = orc.check16(r, ref, dtype)
+            assert bad == 0, (detail, bad, mx, first)
+
+
+def test_dgrad_stream_k(gg, orc):
+    torch = _torch()
+    group_m, n, k = [300, 0, 17, 513], 1000, 1024
+    dy, x, w = orc.make_grad_inputs(group_m, n, k, 0)
+    ref = orc.grouped_dgrad_f32(dy, w, group_m, 0)
+    dyd, wd = upload(torch, dy), upload(torch, w)
+    for kind in (1, 2):
+        dx = torch.zeros(sum(group_m) * k, dtype=torch.int16, device="cuda")
+        b = gg.B200Backend()
+        for key, val in (("variant", 0), ("bn", 256), ("stream_k", kind), ("max_ctas", 10)):
+            b.set_option(key, val)
+        s = torch.cuda.current_stream().cuda_stream
+        assert b.prepare_grad(gg.OP_DGRAD, 0, group_m, n, k, dy_ptr=dyd.data_ptr(), w_ptr=wd.data_ptr(),
+                              dx_ptr=dx.data_ptr(), stream=s) == ""
+        assert "stream_k=" in b.detail(), b.detail()
+        for _ in range(2):
+            b.run(s)
+            assert b.device_status(s) == 0
+            bad, mx, first = orc.check16(dx.cpu().numpy().view(np.uint16).reshape(-1, k), ref, 0)
+            assert bad == 0, (b.detail(), bad, mx, first)
+
+
+def test_stream_k_not_applicable_is_refused(gg, orc):
+    """Forced stream-K on a tiling without a partial last wave (10 CTAs = 5 pairs; 20 tiles)."""
+    torch = _torch()
+    group_m, n, k = [512, 512], 1280, 256  # 2 x 2 m-tiles x 5 n-tiles of 256 = 20 pair tiles
+    x, w = orc.make_inputs(group_m, n, k, 0)
+    xd, wd = upload(torch, x), upload(torch, w)
+    out = torch.zeros(sum(group_m) * n, dtype=torch.int16, device="cuda")
+    b = gg.B200Backend()
+    for key, val in (("variant", 0), ("bn", 256), ("stream_k", 1), ("max_ctas", 10)):
+        b.set_option(key, val)
+    s = torch.cuda.current_stream().cuda_stream
+    why = b.prepare(0, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s)
+    assert "stream_k" in why, why
+
+
+@pytest.mark.parametrize("variant,bn", [(0, 240), (0, 208), (0, 144), (0, 48), (0, 16), (1, 240), (1, 112),
+                                        (1, 16), (2, 80), (2, 16)])
+def test_tile_widths_16_mod_32(gg, orc, variant, bn):
+    """Tile widths that are multiples of 16 but not of 32 end in a half 32-column chunk: it is
+    read whole from TMEM and only its first 16 columns are stored. N = 1000 is not a multiple of
+    any of these widths, so tile-end and tensor-end masking meet."""
+    torch = _torch()
+    group_m, n, k = [300, 0, 17, 513], 1000, 320
+    x, w = orc.make_inputs(group_m, n, k, 1)
+    xd, wd = upload(torch, x), upload(torch, w)
+    got, detail = run_backend(gg, group_m, n, k, 1, xd, wd, variant=variant, bn=bn)
+    assert f"x{bn}x" in detail, detail
+    bad, mx, first = orc.check16(got, orc.grouped_gemm_f32(x, w, group_m, 1), 1)
+    assert bad == 0, (detail, bad, mx, first)
+
+
+@pytest.mark.parametrize("opts", [{"variant": 0, "bn": 240, "split": 2},
+                                  {"variant": 0, "bn": 176, "stream_k": 2, "max_ctas": 10},
+                                  {"variant": 1, "bn": 176, "split": 3, "split_tail": 1, "max_ctas": 10},
+                                  {"variant": 0, "bn": 240, "store": 0},
+                                  {"variant": 0, "bn": 240, "store": 1}])
+def test_tile_widths_16_mod_32_with_partials_and_store_paths(gg, orc, opts):
+    """The half chunk through the split-K / stream-K workspace (whole 32-column blocks, upper half
+    unused) and through both epilogue store paths."""
+    torch = _torch()
+    group_m, n, k = [300, 0, 17, 513], 1000, 1000
+    x, w = orc.make_inputs(group_m, n, k, 0)
+    ref = orc.grouped_gemm_f32(x, w, group_m, 0)
+    xd, wd = upload(torch, x), upload(torch, w)
+    res, detail = _run_opts(gg, torch, group_m, n, k, 0, xd, wd, opts)
+    assert f"x{opts['bn']}x" in detail, detail
+    for r in res:
+        bad, mx, first = orc.check16(r, ref, 0)
+        assert bad == 0, (detail, bad, mx, first)
