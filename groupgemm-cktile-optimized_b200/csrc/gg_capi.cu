@@ -191,12 +191,20 @@ int sk_max_pieces(int64_t sk_tiles, int64_t clusters, int64_t atoms) {
     return int(most);
 }
 
-// Cycles per MMA of one CTA (pair) for a tile width, fitted to B200 measurements for each
-// variant: the tensor pipe needs bn/2 cycles, but the single issuing thread, the per-stage
-// wait/commit and the L2->SM traffic add a part that shrinks slower than bn. For the pair
-// variant, timestamps inside the kernel show a floor of ~130 cycles per instruction below a
-// width of ~200 (and ~150 for the one-atom 1-CTA variant): narrower tiles buy little per MMA.
-double cycles_per_mma(const Variant &v, int bn) {
+// Cycles per MMA of one CTA (pair) for a tile width, fitted to B200 measurements in two regimes.
+// Few waves: the MMA issue keeps pace with the tensor pipe, so an MMA of width bn costs about bn/2
+// cycles plus a small constant (one-wave runs with K = 16384, every width; the one-atom-stage
+// variant a little more). That holds for the pair variant up to three waves of tiles whatever the
+// K; the one-CTA variants keep it only for a short launch (one wave of at most 64 K-atoms per SM,
+// burst clocks): over longer ones they run power-capped and measured 1.5-2x slower per flop than
+// a pair (each SM loads its own B tile). Many waves: the launch runs power-capped and narrow tiles
+// pay for their extra operand traffic per flop; the costs there are the older multi-wave fit, which
+// picks the measured best widths on those shapes (240 over 192 on N = 2880, 256 on L, D, E).
+// `atoms` is the K atoms one cluster works through in the launch.
+double cycles_per_mma(const Variant &v, int bn, int64_t tiles, int slots, double atoms) {
+    const bool few_waves = v.cg == 2 ? tiles <= 3 * int64_t(slots) : tiles <= slots && atoms <= 64.0;
+    if (few_waves)
+        return 0.4 * bn + (v.cg == 1 && v.atoms < 2 ? 26.0 : 24.0);
     if (v.cg == 2)
         return std::max(0.344 * bn + 60.0, 130.0);
     return v.atoms >= 2 ? 0.344 * bn + 63.0 : std::max(0.396 * bn + 70.0, 150.0);
@@ -211,7 +219,6 @@ double cycles_per_mma(const Variant &v, int bn) {
 double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots, int splits, bool hybrid, int sk = 0) {
     const int64_t tiles = tiles_for(p, v, bn);
     const int64_t atoms = (p->k + gg::kBK - 1) / gg::kBK;
-    const double per_mma = cycles_per_mma(v, bn);
     // A CTA pair pays a fixed start-up cost (cluster barrier, cross-CTA pipeline fill) that only
     // matters for launches of a few microseconds.
     double fixed = v.cg == 2 ? 1500.0 : 0.0;
@@ -236,7 +243,7 @@ double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots, in
         // the others back and stores out with direct stores
         fixed += hybrid ? 1000.0 + double(splits - 1) * double(bn) * 12.0 : 2500.0 + double(splits) * double(bn) * 10.0;
     }
-    return unit_atoms * 4.0 * per_mma + fixed;
+    return unit_atoms * 4.0 * cycles_per_mma(v, bn, tiles, slots, unit_atoms) + fixed;
 }
 
 // Pick the variant, tile width and split-K / stream-K form with the smallest modelled time.
@@ -260,8 +267,10 @@ Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_var
         for (int bn = v.bn; bn >= 16; bn -= 16) {
             if (forced_bn > 0 && bn != forced_bn)
                 continue;
-            if (forced_bn <= 0 && bn < 128)
-                continue;  // narrower tiles are issue-bound; only on request
+            if (forced_bn <= 0 && bn < 96)
+                continue;  // narrower tiles only on request
+            if (forced_bn <= 0 && bn < 128 && tiles_for(p, v, bn) > slots)
+                continue;  // below 128 columns only for a one-wave tiling (it fills more SMs)
             // A width in steps of 16 (not 32) only where it tiles N exactly (N = 2880 = 12 x 240
             // against 256's 6.7% padding: +2-9% measured); with a ragged N tail it measured
             // between -5% and +3% against the widths in steps of 32.

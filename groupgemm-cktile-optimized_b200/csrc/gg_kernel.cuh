@@ -18,9 +18,12 @@
 //   * warp 0: TMA producer. 128-byte-swizzled A (128 x 64) and B (BN/kCG x 64) tiles into a
 //     STAGES-deep shared-memory ring guarded by full/empty mbarriers (no multicast: every CTA
 //     loads its own halves);
-//   * warp 1: TMEM allocator and, in the pair leader, the single MMA-issuing thread. The
-//     accumulator lives in Tensor Memory, double-buffered (2 x BN fp32 columns) so the
-//     epilogue of tile i overlaps the main loop of tile i+1;
+//   * warp 1: TMEM allocator and, in the pair leader, the MMA issuer. The accumulator lives in
+//     Tensor Memory, double-buffered (2 x BN fp32 columns) so the epilogue of tile i overlaps
+//     the main loop of tile i+1;
+//   * the producer and MMA warps run their loops converged and one elected lane issues the
+//     single-thread instructions (predicated), which keeps the MMA issue at the tensor pipe's
+//     rate for every tile width;
 //   * warps 2-5: epilogue. tcgen05.ld 32 lanes x 32 columns, fp32 -> bf16/fp16 (RNE), then
 //     per warp 32-row x 64-column boxes through 128-byte-swizzled shared-memory staging and TMA
 //     stores with an evict-first L2 policy (the analogue of the reference's non-temporal C
@@ -333,6 +336,13 @@ __device__ __noinline__ bool wait_count(const int32_t *ctr, int want, const Abor
     }
 }
 
+// Bounded wait by a whole converged warp (the producer and MMA roles): every lane tests the
+// barrier and the warp agrees on the outcome (a wait that ran out in any lane ends the role in all).
+__device__ __forceinline__ bool wait_all(uint32_t bar, uint32_t parity, const Abort &ab, uint32_t code) {
+    const bool ok = wait_one(bar, parity, ab, code);
+    return __all_sync(0xffffffffu, ok ? 1 : 0) != 0;
+}
+
 // Warp-uniform bounded wait: lane 0 waits, the result is broadcast.
 __device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, const Abort &ab, uint32_t code) {
     int ok = 1;
@@ -353,20 +363,21 @@ __device__ __forceinline__ uint32_t pack2(uint32_t a, uint32_t b) {
 }
 
 // Issue one 2-D / 3-D TMA load into this CTA's shared memory, completing on `bar` (in a CTA pair
-// the leader's barrier, through the .cta_group::2 form).
+// the leader's barrier, through the .cta_group::2 form); only in the lane where `pred` != 0.
 template <int kCG>
-__device__ __forceinline__ void load_2d(uint32_t dst, const void *map, uint32_t bar, int c0, int c1) {
+__device__ __forceinline__ void load_2d(uint32_t dst, const void *map, uint32_t bar, int c0, int c1, uint32_t pred) {
     if constexpr (kCG == 1)
-        ptx::tma_load_2d(dst, map, bar, c0, c1);
+        ptx::tma_load_2d(dst, map, bar, c0, c1, pred);
     else
-        ptx::tma_load_2d_pair(dst, map, bar, c0, c1);
+        ptx::tma_load_2d_pair(dst, map, bar, c0, c1, pred);
 }
 template <int kCG>
-__device__ __forceinline__ void load_3d(uint32_t dst, const void *map, uint32_t bar, int c0, int c1, int c2) {
+__device__ __forceinline__ void load_3d(uint32_t dst, const void *map, uint32_t bar, int c0, int c1, int c2,
+                                        uint32_t pred) {
     if constexpr (kCG == 1)
-        ptx::tma_load_3d(dst, map, bar, c0, c1, c2);
+        ptx::tma_load_3d(dst, map, bar, c0, c1, c2, pred);
     else
-        ptx::tma_load_3d_pair(dst, map, bar, c0, c1, c2);
+        ptx::tma_load_3d_pair(dst, map, bar, c0, c1, c2, pred);
 }
 
 constexpr int kMnBoxBytes = 64 * kBK * 2;  // one MN-major box: 64 MN x 64 K elements
@@ -461,8 +472,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // per group.)
 
     if (warp == 0) {
-        // ---------------- TMA producer (one thread) ----------------
-        if (lane == 0) {
+        // ---------------- TMA producer (warp 0) ----------------
+        // The warp runs the loop converged; one elected lane issues the barrier arrive and the TMA
+        // loads (predicated instructions, no divergent branch around them).
+        {
+            const uint32_t issue = ptx::elect_one_sync();
             const uint32_t full_leader0 = kCG == 2 ? ptx::mapa(full_bar(0), 0) : full_bar(0);
             int cursor = 0;
             int s = 0;
@@ -491,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 for (int ks = 0; ks < num_ks; ++ks) {
-                    if (!wait_one(empty_bar(s), ph ^ 1u, ab, kStatusTimeout | kRoleProducer | uint32_t(s))) {
+                    if (!wait_all(empty_bar(s), ph ^ 1u, ab, kStatusTimeout | kRoleProducer | uint32_t(s))) {
                         ok = false;
                         break;
                     }
@@ -502,8 +516,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t fb = full_leader0 + 8u * s;
                     // test hook: the leader skips its arrive and loads of cluster 0's first stage
                     const bool skip = p.test_stall != 0 && cluster_id == 0 && leader && ks == 0 && i == 0;
-                    if (leader && !skip)
-                        ptx::mbar_arrive_expect_tx(full_bar(s), uint32_t(kCG * na * (C::kAAtomBytes + b_rows * kBK * 2)));
+                    ptx::mbar_arrive_expect_tx(full_bar(s), uint32_t(kCG * na * (C::kAAtomBytes + b_rows * kBK * 2)),
+                                               leader && !skip ? issue : 0u);
 #pragma unroll
                     for (int a = 0; a < kAtoms; ++a) {
                         if (a < na && !skip) {
@@ -512,19 +526,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const uint32_t bd = b_dst + a * C::kBAtomBytes;
                             if constexpr (kAMn) {
                                 // wgrad A = dy^T: two 64-column boxes of the group's dy rows
-                                load_2d<kCG>(ad, map_a, fb, a_row, k0);
-                                load_2d<kCG>(ad + kMnBoxBytes, map_a, fb, a_row + 64, k0);
+                                load_2d<kCG>(ad, map_a, fb, a_row, k0, issue);
+                                load_2d<kCG>(ad + kMnBoxBytes, map_a, fb, a_row + 64, k0, issue);
                             } else {
-                                load_2d<kCG>(ad, map_a, fb, k0, a_row);
+                                load_2d<kCG>(ad, map_a, fb, k0, a_row, issue);
                             }
                             if constexpr (kOp == kOpForward) {
-                                load_3d<kCG>(bd, map_b, fb, k0, b_row, tc.g);
+                                load_3d<kCG>(bd, map_b, fb, k0, b_row, tc.g, issue);
                             } else {
                                 for (int j = 0; j < b_rows / 64; ++j) {
                                     if constexpr (kOp == kOpDgrad)  // w[g] rows k0.., columns b_row + 64j..
-                                        load_3d<kCG>(bd + j * kMnBoxBytes, map_b, fb, b_row + 64 * j, k0, tc.g);
+                                        load_3d<kCG>(bd + j * kMnBoxBytes, map_b, fb, b_row + 64 * j, k0, tc.g, issue);
                                     else  // x rows (tokens) k0.. of the group, columns b_row + 64j..
-                                        load_2d<kCG>(bd + j * kMnBoxBytes, map_b, fb, b_row + 64 * j, k0);
+                                        load_2d<kCG>(bd + j * kMnBoxBytes, map_b, fb, b_row + 64 * j, k0, issue);
                                 }
                             }
                         }
@@ -537,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // Tail: every stage released, so no tcgen05.commit is still in flight to this CTA.
             for (int i = 0; ok && i < C::kStages; ++i) {
-                ok = wait_one(empty_bar(s), ph ^ 1u, ab, kStatusTimeout | kRoleProducer | 0x80u);
+                ok = wait_all(empty_bar(s), ph ^ 1u, ab, kStatusTimeout | kRoleProducer | 0x80u);
                 if (++s == C::kStages) {
                     s = 0;
                     ph ^= 1u;
@@ -546,8 +560,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ---------------- MMA issuer (one thread of the pair leader) ----------------
-        if (leader && lane == 0) {
+        // ---------------- MMA issuer (warp 1 of the pair leader) ----------------
+        // The warp runs the loop converged; one elected lane issues the tcgen05.mma and
+        // tcgen05.commit instructions (predicated), which keeps the issue at the tensor pipe's rate.
+        if (leader) {
+            const uint32_t issue = ptx::elect_one_sync();
             uint32_t tl = 0;
             int s = 0;
             uint32_t ph = 0;
@@ -565,14 +582,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t acc_ph = (tl >> 1) & 1u;
                 // The epilogue warps (also the peer's) arrive after tcgen05.wait::ld, so their reads of
                 // this accumulator are complete; a CTA-scope wait is enough before overwriting it.
-                if (!wait_one(tempty_bar(acc), acc_ph ^ 1u, ab, kStatusTimeout | kRoleMma | 0x40u | uint32_t(acc))) {
+                if (!wait_all(tempty_bar(acc), acc_ph ^ 1u, ab, kStatusTimeout | kRoleMma | 0x40u | uint32_t(acc))) {
                     ok = false;
                     break;
                 }
                 ptx::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + uint32_t(acc * kBN);
                 for (int ks = 0; ks < num_ks; ++ks) {
-                    if (!wait_one(full_bar(s), ph, ab, kStatusTimeout | kRoleMma | uint32_t(s))) {
+                    if (!wait_all(full_bar(s), ph, ab, kStatusTimeout | kRoleMma | uint32_t(s))) {
                         ok = false;
                         break;
                     }
@@ -594,13 +611,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 const uint64_t da = uint64_t((a * C::kAAtomBytes + kk * kStepA) >> 4);
                                 const uint64_t db = uint64_t((a * C::kBAtomBytes + kk * kStepB) >> 4);
                                 ptx::umma_f16<kCG>(d_tmem, adesc + da, bdesc + db, idesc,
-                                                   (ks | a | kk) != 0 ? 1u : 0u);
+                                                   (ks | a | kk) != 0 ? 1u : 0u, issue);
                             }
                         }
                     }
-                    ptx::umma_commit<kCG>(empty_bar(s));
+                    ptx::umma_commit<kCG>(empty_bar(s), issue);
                     if constexpr (kCG == 2)
-                        ptx::umma_commit<kCG>(ptx::mapa(empty_bar(s), 1));
+                        ptx::umma_commit<kCG>(ptx::mapa(empty_bar(s), 1), issue);
                     if (++s == C::kStages) {
                         s = 0;
                         ph ^= 1u;
@@ -608,13 +625,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!ok)
                     break;
-                ptx::umma_commit<kCG>(tfull_bar(acc));
+                ptx::umma_commit<kCG>(tfull_bar(acc), issue);
                 if constexpr (kCG == 2)
-                    ptx::umma_commit<kCG>(ptx::mapa(tfull_bar(acc), 1));
+                    ptx::umma_commit<kCG>(ptx::mapa(tfull_bar(acc), 1), issue);
             }
             // Tail: both accumulators released by every epilogue warp of the pair.
             for (uint32_t i = tl; ok && i < tl + 2; ++i)
-                ok = wait_one(tempty_bar(int(i & 1u)), ((i >> 1) & 1u) ^ 1u, ab, kStatusTimeout | kRoleMma | 0x80u);
+                ok = wait_all(tempty_bar(int(i & 1u)), ((i >> 1) & 1u) ^ 1u, ab, kStatusTimeout | kRoleMma | 0x80u);
         }
         __syncwarp();
     } else {

@@ -24,6 +24,14 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
     return r;
 }
 
+// One lane of the (converged) warp: 1 there, 0 in the others. The warp keeps running the issuing
+// code together and predicates the single-thread instructions (TMA, MMA, commit) on this value.
+__device__ __forceinline__ uint32_t elect_one_sync() {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\tselp.b32 %0, 1, 0, e;\n\t}" : "=r"(r));
+    return r;
+}
+
 __device__ __forceinline__ uint64_t globaltimer() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -72,8 +80,10 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+// Executed only where `pred` != 0 (the other lanes of the warp pass over it).
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes, uint32_t pred) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t"
+                 "@q mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t}" ::"r"(bar), "r"(bytes), "r"(pred)
                  : "memory");
 }
 
@@ -113,6 +123,8 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 }
 
 // ---- TMA (tensor) loads: global -> shared, completion counted on an mbarrier ----
+// The load wrappers issue only where `pred` != 0, so a converged warp can run the producer loop
+// with one elected lane issuing.
 __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
@@ -124,36 +136,40 @@ __device__ __forceinline__ void fence_tensormap_acquire(const void *tmap) {
 }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, uint32_t bar, int32_t c0,
-                                            int32_t c1) {
-    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-                 "l"(tmap), "r"(bar), "r"(c0), "r"(c1)
+                                            int32_t c1, uint32_t pred) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+                 "@q cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4}], [%2];\n\t}" ::"r"(dst),
+                 "l"(tmap), "r"(bar), "r"(c0), "r"(c1), "r"(pred)
                  : "memory");
 }
 
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, uint32_t bar, int32_t c0,
-                                            int32_t c1, int32_t c2) {
-    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-                 "l"(tmap), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+                                            int32_t c1, int32_t c2, uint32_t pred) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %6, 0;\n\t"
+                 "@q cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4, %5}], [%2];\n\t}" ::"r"(dst),
+                 "l"(tmap), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(pred)
                  : "memory");
 }
 
 // CTA-pair forms: the destination is this CTA's shared memory, the completion barrier may be
 // the pair leader's (a shared::cluster address from mapa). No multicast.
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void *tmap, uint32_t bar,
-                                                 int32_t c0, int32_t c1) {
-    asm volatile("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-                 "l"(tmap), "r"(bar), "r"(c0), "r"(c1)
+                                                 int32_t c0, int32_t c1, uint32_t pred) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+                 "@q cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4}], [%2];\n\t}" ::"r"(dst),
+                 "l"(tmap), "r"(bar), "r"(c0), "r"(c1), "r"(pred)
                  : "memory");
 }
 
 __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void *tmap, uint32_t bar,
-                                                 int32_t c0, int32_t c1, int32_t c2) {
-    asm volatile("cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-                 "l"(tmap), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+                                                 int32_t c0, int32_t c1, int32_t c2, uint32_t pred) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %6, 0;\n\t"
+                 "@q cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4, %5}], [%2];\n\t}" ::"r"(dst),
+                 "l"(tmap), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(pred)
                  : "memory");
 }
 
@@ -304,29 +320,38 @@ __host__ __device__ constexpr uint32_t f16_idesc(uint32_t ab_fmt, int m, int n, 
            (uint32_t(m >> 4) << 24);
 }
 
+// Issued only where `pred` != 0: the MMA warp runs its loop converged and one elected lane
+// issues. (Measured on B200: issued this way a pair MMA of width N takes the tensor pipe's N/2
+// cycles for every N, with a commit every 4 or 8 MMAs; issued from a lone lane inside a divergent
+// branch the same loop takes ~120-130 cycles per MMA below N = 256.)
 template <int kCG>
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
+                                         uint32_t accumulate, uint32_t pred) {
     if constexpr (kCG == 1)
-        asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                     "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-                     "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+                     "@q tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                     "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(pred)
                      : "memory");
     else
-        asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                     "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-                     "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+                     "@q tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                     "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(pred)
                      : "memory");
 }
 
 // Arrive (once) on `bar` when all tcgen05.mma issued so far by this thread have completed.
-// `bar` is a shared::cluster address, so it may name the peer CTA's barrier.
-template <int kCG> __device__ __forceinline__ void umma_commit(uint32_t bar) {
+// `bar` is a shared::cluster address, so it may name the peer CTA's barrier. Only where
+// `pred` != 0 (the lane that issued the MMAs).
+template <int kCG> __device__ __forceinline__ void umma_commit(uint32_t bar, uint32_t pred) {
     if constexpr (kCG == 1)
-        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+        asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t"
+                     "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar),
+                     "r"(pred)
                      : "memory");
     else
-        asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+        asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t"
+                     "@q tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar),
+                     "r"(pred)
                      : "memory");
 }
 
