@@ -306,7 +306,7 @@ __device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, const Abor
     }
 }
 
-// Bounded wait by one thread: an inline first test, the loop out of line.
+// Bounded wait in the calling thread: an inline first test, the loop out of line.
 template <bool kClusterScope = false>
 __device__ __forceinline__ bool wait_one(uint32_t bar, uint32_t parity, const Abort &ab, uint32_t code) {
     if (kClusterScope ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity))
@@ -482,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            int fenced_g = -1;  // wgrad: group whose tensor maps this thread has acquired
+            int fenced_g = -1;  // wgrad: group whose tensor maps the warp has acquired
             for (int i = 0; i < units.n && ok; ++i) {
                 const Unit un = unit_at(p, units, cluster_id, num_clusters, i);
                 const TileCoord tc = decode_tile<C::kClusterM, kOp>(p, un.t, cursor);
