@@ -19,6 +19,7 @@
 
 #include "gg_b200.h"
 #include "gg_kernel.cuh"
+#include "gg_sched.h"
 
 #ifndef GG_ATOMS_V0
 #define GG_ATOMS_V0 2
@@ -170,27 +171,6 @@ struct Choice {
                   // one full wave more
 };
 
-// Stream-K region of a launch: the first `sk_tiles` tiles, whose K atoms are dealt out evenly to
-// the `clusters` clusters. kind 1: the tiles that would form a partial last wave (tiles % clusters);
-// kind 2: those plus one full wave, so that each cluster's range spans at least one tile. Returns 0
-// when the kind does not apply (no partial wave, too few tiles, or fewer atoms than clusters).
-int64_t sk_tiles_for(int64_t tiles, int64_t clusters, int64_t atoms, int kind) {
-    const int64_t rem = tiles % clusters;
-    const int64_t sk = kind == 1 ? rem : kind == 2 && rem > 0 && tiles >= rem + clusters ? rem + clusters : 0;
-    return sk > 0 && sk * atoms >= clusters ? sk : 0;
-}
-
-// Most pieces any stream-K tile is cut into (cluster c's range is [c S / C, (c+1) S / C)); the
-// kernel's workspace stride and the length of its longest fix-up.
-int sk_max_pieces(int64_t sk_tiles, int64_t clusters, int64_t atoms) {
-    const int64_t S = sk_tiles * atoms;
-    auto cluster_of = [&](int64_t g) { return ((g + 1) * clusters - 1) / S; };
-    int64_t most = 1;
-    for (int64_t t = 0; t < sk_tiles; ++t)
-        most = std::max(most, cluster_of((t + 1) * atoms - 1) - cluster_of(t * atoms) + 1);
-    return int(most);
-}
-
 // Cycles per MMA of one CTA (pair) for a tile width, fitted to B200 measurements in two regimes.
 // Few waves: the MMA issue keeps pace with the tensor pipe, so an MMA of width bn costs about bn/2
 // cycles plus a small constant (one-wave runs with K = 16384, every width; the one-atom-stage
@@ -228,10 +208,10 @@ double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots, in
         // writes an fp32 partial and reads one back at about the same time, so the fix-up runs at
         // the GPU-wide store rate: timestamps inside the kernel show ~3.5-5 us per 128 x 240 fp32
         // partial per CTA (~16 bytes per cycle per SM) plus ~2 us of fence and arrival latency.
-        const int64_t skt = sk_tiles_for(tiles, slots, atoms, sk);
+        const int64_t skt = gg::sk_tiles_for(tiles, slots, atoms, sk);
         const int64_t S = skt * atoms;
         unit_atoms = double((tiles - skt) / slots) * double(atoms) + double((S + slots - 1) / slots);
-        fixed += 4000.0 + double(sk_max_pieces(skt, slots, atoms) - 1) * double(bn) * 64.0;
+        fixed += 4000.0 + double(gg::sk_max_pieces(skt, slots, atoms) - 1) * double(bn) * 64.0;
     } else if (splits <= 1) {
         unit_atoms = double((tiles + slots - 1) / slots) * double(atoms);
     } else {
@@ -283,10 +263,10 @@ Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_var
             for (int kind = 1; kind <= 2 && min_splits == 1 && stream_k != 0; ++kind) {
                 if (stream_k > 0 && kind != stream_k)
                     continue;
-                const int64_t skt = sk_tiles_for(tiles, slots, atoms, kind);
+                const int64_t skt = gg::sk_tiles_for(tiles, slots, atoms, kind);
                 if (skt == 0)
                     continue;
-                const int pieces = sk_max_pieces(skt, slots, atoms);
+                const int pieces = gg::sk_max_pieces(skt, slots, atoms);
                 // automatic: at most 4 pieces per tile and >= 4 atoms per cluster
                 if (stream_k < 0 && (pieces > 4 || skt * atoms < 4 * int64_t(slots)))
                     continue;
@@ -632,7 +612,7 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     // Stream-K instead: the first sk_tiles tiles' atoms dealt out evenly to every cluster.
     const int64_t clusters = std::max(1, v.cg == 2 ? pairs : num_sms);
     const int64_t atoms = (cm.k + gg::kBK - 1) / gg::kBK;
-    const int64_t sk_tiles = ch.sk > 0 ? sk_tiles_for(tiles, clusters, atoms, ch.sk) : 0;
+    const int64_t sk_tiles = ch.sk > 0 ? gg::sk_tiles_for(tiles, clusters, atoms, ch.sk) : 0;
     const bool partials = ch.splits > 1 || sk_tiles > 0;  // fp32 workspace + arrival counters
     const int64_t split_tiles = sk_tiles > 0 ? sk_tiles : ch.splits > 1 ? (ch.hybrid ? tiles % clusters : tiles) : 0;
     const int64_t units = sk_tiles > 0 ? clusters : tiles + split_tiles * (ch.splits - 1);

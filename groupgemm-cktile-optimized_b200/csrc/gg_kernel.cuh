@@ -222,13 +222,14 @@ __device__ __forceinline__ TileCoord decode_tile(const KernelParams &p, int t, i
 //     sk_tiles + c, sk_tiles + c + C, ... Every cluster gets the same number of atoms (+-1),
 //     whatever the number of tiles.
 // Either way the pieces of a tile come first in each cluster's list, so the fix-up runs in the
-// epilogue warps while the MMA warp works on what follows.
+// epilogue warps while the MMA warp works on what follows. (Host-callable as well, so that a CPU
+// test can walk the exact schedule: tests/test_schedule.py.)
 struct Unit {
     int t, atom0, atom1, piece, npieces;
 };
 
 // Stream-K: the cluster whose range holds atom g (S = atoms in the stream-K region; S >= C).
-__device__ __forceinline__ int sk_cluster_of(int64_t g, int64_t S, int C) { return int(((g + 1) * C - 1) / S); }
+__host__ __device__ __forceinline__ int sk_cluster_of(int64_t g, int64_t S, int C) { return int(((g + 1) * C - 1) / S); }
 
 struct UnitList {
     int n;              // units of this cluster
@@ -236,7 +237,7 @@ struct UnitList {
     int64_t sk0, sk1;   // stream-K: this cluster's atom range
 };
 
-__device__ __forceinline__ UnitList units_of(const KernelParams &p, int c, int C) {
+__host__ __device__ __forceinline__ UnitList units_of(const KernelParams &p, int c, int C) {
     UnitList l{0, 0, 0, 0};
     if (p.sk_tiles > 0) {
         const int64_t A = p.num_kb, S = int64_t(p.sk_tiles) * A;
@@ -253,7 +254,7 @@ __device__ __forceinline__ UnitList units_of(const KernelParams &p, int c, int C
     return l;
 }
 
-__device__ __forceinline__ Unit unit_at(const KernelParams &p, const UnitList &l, int c, int C, int i) {
+__host__ __device__ __forceinline__ Unit unit_at(const KernelParams &p, const UnitList &l, int c, int C, int i) {
     const int A = p.num_kb;
     if (p.sk_tiles > 0) {
         if (i < l.n_sk) {

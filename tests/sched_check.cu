@@ -1,0 +1,129 @@
+// CPU check of the kernel's work-unit schedule (built and run by tests/test_schedule.py).
+//
+// It calls the same units_of / unit_at the kernel runs on the device (gg_kernel.cuh, host-callable)
+// and the host-side stream-K arithmetic the library sizes the launch with (gg_sched.h), for every
+// cluster of random launches of each schedule form the library produces: whole tiles, plain
+// split-K, split-K of the partial last wave, and stream-K of kind 1 and 2. For each launch:
+//   * every (tile, K atom) is covered by exactly one unit, and every unit is non-empty;
+//   * the pieces of a tile are numbered 0..n-1 in K order and agree on n (the fixed summation order);
+//   * a tile cut into pieces has workspace: n <= splits (the stride) and the tile is a split tile;
+//   * stream-K: every piece but piece 0 is the first unit of its cluster, so the fixed summer
+//     (piece 0) only ever waits for units that wait on nothing themselves (no circular wait).
+// Prints "ok <launches> <units>" and exits 0, or prints the first violation and exits 1.
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <vector>
+
+#include "gg_kernel.cuh"
+#include "gg_sched.h"
+
+namespace {
+
+struct Rng {
+    uint64_t s;
+    uint64_t next() {
+        s ^= s << 13;
+        s ^= s >> 7;
+        s ^= s << 17;
+        return s;
+    }
+    int range(int lo, int hi) { return lo + int(next() % uint64_t(hi - lo + 1)); }  // [lo, hi]
+};
+
+struct Seen {
+    int piece, npieces, atom0, atom1, cluster, index;
+};
+
+bool fail(const char *what, int form, int64_t tiles, int C, int A, int s, int t) {
+    std::printf("FAIL %s: form %d tiles %lld clusters %d atoms %d splits %d tile %d\n", what, form, (long long)tiles,
+                C, A, s, t);
+    return false;
+}
+
+// One launch: form 0 whole tiles, 1 plain split-K, 2 last-wave split-K, 3 / 4 stream-K kind 1 / 2.
+bool check(int form, int64_t tiles, int slots, int A, int s, long long &units_seen) {
+    gg::KernelParams p{};
+    p.total_tiles = int32_t(tiles);
+    p.num_kb = A;
+    int C = slots;
+    if (form == 0) {
+        p.splits = 1;
+    } else if (form == 1 || form == 2) {
+        p.splits = s;
+        p.split_tiles = int32_t(form == 1 ? tiles : tiles % slots);
+        const int64_t units = tiles + int64_t(p.split_tiles) * (s - 1);
+        C = int(std::min<int64_t>(slots, units));  // the launch's grid, as prepare sizes it
+    } else {
+        const int64_t sk = gg::sk_tiles_for(tiles, slots, A, form == 3 ? 1 : 2);
+        if (sk == 0)
+            return true;  // the library refuses this kind for this tiling
+        p.sk_tiles = int32_t(sk);
+        p.splits = gg::sk_max_pieces(sk, slots, A);
+    }
+    std::vector<std::vector<Seen>> by_tile(static_cast<std::size_t>(tiles));
+    for (int c = 0; c < C; ++c) {
+        const gg::UnitList l = gg::units_of(p, c, C);
+        for (int i = 0; i < l.n; ++i) {
+            const gg::Unit u = gg::unit_at(p, l, c, C, i);
+            if (u.t < 0 || u.t >= tiles)
+                return fail("tile index out of range", form, tiles, C, A, s, u.t);
+            if (!(0 <= u.atom0 && u.atom0 < u.atom1 && u.atom1 <= A))
+                return fail("empty or out-of-range K range", form, tiles, C, A, s, u.t);
+            by_tile.at(static_cast<std::size_t>(u.t)).push_back({u.piece, u.npieces, u.atom0, u.atom1, c, i});
+            ++units_seen;
+        }
+    }
+    for (int64_t t = 0; t < tiles; ++t) {
+        std::vector<Seen> v = by_tile.at(static_cast<std::size_t>(t));
+        if (v.empty())
+            return fail("tile not covered", form, tiles, C, A, s, int(t));
+        std::sort(v.begin(), v.end(), [](const Seen &a, const Seen &b) { return a.atom0 < b.atom0; });
+        int at = 0;
+        const int n = v[0].npieces;
+        for (size_t j = 0; j < v.size(); ++j) {
+            if (v[j].atom0 != at)
+                return fail("K atoms missing or covered twice", form, tiles, C, A, s, int(t));
+            at = v[j].atom1;
+            if (v[j].npieces != n || v[j].piece != int(j))
+                return fail("pieces not numbered 0..n-1 in K order", form, tiles, C, A, s, int(t));
+        }
+        if (at != A || int(v.size()) != n)
+            return fail("K range not covered to the end", form, tiles, C, A, s, int(t));
+        if (n > 1) {
+            const bool split_tile = p.sk_tiles > 0 ? t < p.sk_tiles : t < p.split_tiles;
+            if (!split_tile || n > p.splits)
+                return fail("pieces without workspace", form, tiles, C, A, s, int(t));
+            if (p.sk_tiles > 0)
+                for (size_t j = 1; j < v.size(); ++j)
+                    if (v[j].index != 0)
+                        return fail("stream-K piece > 0 not first in its cluster", form, tiles, C, A, s, int(t));
+        }
+    }
+    return true;
+}
+
+}  // namespace
+
+int main(int argc, char **argv) {
+    const int launches = argc > 1 ? std::atoi(argv[1]) : 20000;
+    Rng rng{0x9E3779B97F4A7C15ull};
+    long long units = 0;
+    int done = 0;
+    for (int n = 0; n < launches; ++n) {
+        const int form = n % 5;
+        const int slots = rng.range(1, 3) == 1 ? rng.range(1, 12) : rng.range(60, 148);
+        const int64_t tiles = rng.range(1, 3) == 1 ? rng.range(1, 2 * slots) : rng.range(1, 9000);
+        const int A = rng.range(1, 300);
+        const int s = std::max(2, std::min(A, rng.range(2, 8)));  // the library refuses s > A
+        if ((form == 1 || form == 2) && A < 2)
+            continue;
+        if (form == 2 && (tiles < slots || tiles % slots == 0))
+            continue;  // no partial last wave: the library does not use this form
+        if (!check(form, tiles, slots, A, s, units))
+            return 1;
+        ++done;
+    }
+    std::printf("ok %d %lld\n", done, units);
+    return 0;
+}
