@@ -172,15 +172,25 @@ struct TileCoord {
 //   raster 1: bands of `band` n-tiles; all m-tiles of a band are visited n-fastest, so the band's
 //             weight panels stay in L2 and each activation row block is read from DRAM once per
 //             band (with one band covering every n-tile: each operand once).
+// Read-only load of the group tables: through the read-only data cache on the device, a plain load
+// on the host (where the CPU schedule test walks decode_tile over host arrays).
+__host__ __device__ __forceinline__ int32_t ld_table(const int32_t *q) {
+#ifdef __CUDA_ARCH__
+    return __ldg(q);
+#else
+    return *q;
+#endif
+}
+
 template <int kClusterM, int kOp>
-__device__ __forceinline__ TileCoord decode_tile(const KernelParams &p, int t, int &cursor) {
-    while (__ldg(&p.tile_off[cursor + 1]) <= t)
+__host__ __device__ __forceinline__ TileCoord decode_tile(const KernelParams &p, int t, int &cursor) {
+    while (ld_table(&p.tile_off[cursor + 1]) <= t)
         ++cursor;
     TileCoord tc;
     tc.g = cursor;
-    const int local = t - __ldg(&p.tile_off[tc.g]);
-    const int r0 = __ldg(&p.row_off[tc.g]);
-    const int m = __ldg(&p.row_off[tc.g + 1]) - r0;
+    const int local = t - ld_table(&p.tile_off[tc.g]);
+    const int r0 = ld_table(&p.row_off[tc.g]);
+    const int m = ld_table(&p.row_off[tc.g + 1]) - r0;
     if constexpr (kOp == kOpWgrad) {
         tc.rows = p.tile_rows;
         tc.out_row0 = tc.g * p.tile_rows;

@@ -9,7 +9,9 @@
 //   * a tile cut into pieces has workspace: n <= splits (the stride) and the tile is a split tile;
 //   * stream-K: every piece but piece 0 is the first unit of its cluster, so the fixed summer
 //     (piece 0) only ever waits for units that wait on nothing themselves (no circular wait).
-// Prints "ok <launches> <units>" and exits 0, or prints the first violation and exits 1.
+// Then decode_tile, for random group sizes (empty groups included), widths, bands and both raster
+// orders: tile indices map onto every (group, m-tile, n-tile) exactly once.
+// Prints "ok <launches> <units> <tables>" and exits 0, or prints the first violation and exits 1.
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
@@ -103,6 +105,58 @@ bool check(int form, int64_t tiles, int slots, int A, int s, long long &units_se
     return true;
 }
 
+// decode_tile over one launch's group tables: tiles 0..total-1 map onto every (group, m-tile,
+// n-tile) of the non-empty groups exactly once, with the group's row range, for a raster order
+// and band; walked in order with one cursor (as each role does) and from a fresh cursor.
+template <int kCM, int kOp>
+bool check_decode(const std::vector<int64_t> &group_m, int tiles_n, int band, int raster, int tile_rows) {
+    const int G = int(group_m.size());
+    std::vector<int32_t> tile_off(G + 1), row_off(G + 1);
+    int64_t tiles = 0, rows = 0;
+    for (int g = 0; g < G; ++g) {
+        tile_off[g] = int32_t(tiles);
+        row_off[g] = int32_t(rows);
+        const int64_t tile_rows_g = kOp == gg::kOpWgrad ? tile_rows : group_m[g];
+        tiles += (tile_rows_g + kCM - 1) / kCM * tiles_n;
+        rows += group_m[g];
+    }
+    tile_off[G] = int32_t(tiles);
+    row_off[G] = int32_t(rows);
+    gg::KernelParams p{};
+    p.tile_off = tile_off.data();
+    p.row_off = row_off.data();
+    p.tiles_n = tiles_n;
+    p.band = band;
+    p.raster = raster;
+    p.num_kb = 7;
+    p.tile_rows = tile_rows;
+    std::vector<char> hit(size_t(tiles), 0);
+    int cursor = 0;
+    for (int64_t t = 0; t < tiles; ++t) {
+        const gg::TileCoord tc = gg::decode_tile<kCM, kOp>(p, int(t), cursor);
+        int fresh = 0;
+        const gg::TileCoord tf = gg::decode_tile<kCM, kOp>(p, int(t), fresh);
+        const int g = tc.g;
+        const int64_t m_rows = kOp == gg::kOpWgrad ? tile_rows : group_m[size_t(g)];
+        const int tiles_m = int((m_rows + kCM - 1) / kCM);
+        const bool ok = g >= 0 && g < G && tc.mt >= 0 && tc.mt < tiles_m && tc.nt >= 0 && tc.nt < tiles_n &&
+                        tc.rows == int(m_rows) &&
+                        tc.out_row0 == (kOp == gg::kOpWgrad ? g * tile_rows : row_off[size_t(g)]) &&
+                        tf.g == tc.g && tf.mt == tc.mt && tf.nt == tc.nt;
+        if (!ok) {
+            std::printf("FAIL decode_tile: cm %d op %d G %d tiles_n %d band %d raster %d tile %lld\n", kCM, kOp, G,
+                        tiles_n, band, raster, (long long)t);
+            return false;
+        }
+        const int64_t idx = tile_off[size_t(g)] + int64_t(tc.mt) * tiles_n + tc.nt;
+        if (hit.at(static_cast<std::size_t>(idx))++) {
+            std::printf("FAIL decode_tile: tile (%d, %d, %d) decoded twice\n", g, tc.mt, tc.nt);
+            return false;
+        }
+    }
+    return true;
+}
+
 }  // namespace
 
 int main(int argc, char **argv) {
@@ -124,6 +178,21 @@ int main(int argc, char **argv) {
             return 1;
         ++done;
     }
-    std::printf("ok %d %lld\n", done, units);
+    int decoded = 0;
+    for (int n = 0; n < launches / 10; ++n) {
+        std::vector<int64_t> gm(size_t(rng.range(1, 24)));
+        for (auto &m : gm)
+            m = rng.range(1, 4) == 1 ? 0 : rng.range(1, 3000);
+        const int tiles_n = rng.range(1, 40), band = rng.range(1, 20), raster = rng.range(0, 1);
+        const int tile_rows = rng.range(1, 1500);
+        const bool ok = check_decode<256, gg::kOpForward>(gm, tiles_n, band, raster, tile_rows) &&
+                        check_decode<128, gg::kOpForward>(gm, tiles_n, band, raster, tile_rows) &&
+                        check_decode<256, gg::kOpWgrad>(gm, tiles_n, band, raster, tile_rows) &&
+                        check_decode<128, gg::kOpDgrad>(gm, tiles_n, band, raster, tile_rows);
+        if (!ok)
+            return 1;
+        ++decoded;
+    }
+    std::printf("ok %d %lld %d\n", done, units, decoded);
     return 0;
 }

@@ -6,8 +6,10 @@ random launches of each schedule form (whole tiles, plain split-K, split-K of th
 wave, stream-K of kind 1 and 2). It checks that every (tile, K atom) is covered exactly once,
 that a tile's pieces are numbered in K order (the fixed order the partial sums are added in),
 that a tile in pieces has workspace, and that the stream-K summer only waits for pieces that
-are the first unit of their cluster (no circular wait). The GPU parity tests check the same
-schedules through their results; this walks far more shapes than a GPU run can.
+are the first unit of their cluster (no circular wait). It also walks the kernel's `decode_tile`
+over random group tables (empty groups, both raster orders, every band) and checks that tile
+indices cover every (group, m-tile, n-tile) exactly once. The GPU parity tests check the same
+code through their results; this walks far more shapes than a GPU run can.
 """
 import os
 import shutil
