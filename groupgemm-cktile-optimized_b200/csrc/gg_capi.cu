@@ -82,6 +82,17 @@ const Variant &variant_at(int i) {
 }
 constexpr int kNumVariants = 3;
 
+// The variants' shapes for the cost model (gg_sched.h).
+const gg::TileShape *tile_shapes() {
+    static const gg::TileShape t[kNumVariants] = {
+        {variant_at(0).cg, variant_at(0).bn, variant_at(0).cluster_m, variant_at(0).atoms},
+        {variant_at(1).cg, variant_at(1).bn, variant_at(1).cluster_m, variant_at(1).atoms},
+        {variant_at(2).cg, variant_at(2).bn, variant_at(2).cluster_m, variant_at(2).atoms}};
+    return t;
+}
+
+using gg::Choice;
+
 }  // namespace
 
 struct gg_handle {
@@ -153,159 +164,6 @@ int refuse(gg_handle *h, char *why, size_t why_len, const char *msg) {
         if (e_ != cudaSuccess)                                                                            \
             return fail((h), GG_ERR_CUDA, "%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__); \
     } while (0)
-
-int64_t tiles_for(const gg_problem *p, const Variant &v, int bn) {
-    const int64_t tn = (p->n + bn - 1) / bn;
-    int64_t t = 0;
-    for (int g = 0; g < p->group_num; ++g)
-        t += (p->group_m[g] + v.cluster_m - 1) / v.cluster_m * tn;
-    return t;
-}
-
-struct Choice {
-    int variant;
-    int bn;
-    int splits;
-    bool hybrid;  // splits > 1: only tiles % slots tiles are split (what would be a partial last wave)
-    int sk;       // stream-K: 0 none, 1 over the tiles of the partial last wave, 2 over those and
-                  // one full wave more
-};
-
-// Cycles per MMA of one CTA (pair) for a tile width, fitted to B200 measurements in two regimes.
-// Few waves: the MMA issue keeps pace with the tensor pipe, so an MMA of width bn costs about bn/2
-// cycles plus a small constant (one-wave runs with K = 16384, every width; the one-atom-stage
-// variant a little more). That holds for the pair variant up to three waves of tiles whatever the
-// K; the one-CTA variants keep it only for a short launch (one wave of at most 64 K-atoms per SM,
-// burst clocks): over longer ones they run power-capped and measured 1.5-2x slower per flop than
-// a pair (each SM loads its own B tile). Many waves: the launch runs power-capped and narrow tiles
-// pay for their extra operand traffic per flop; the costs there are the older multi-wave fit, which
-// picks the measured best widths on those shapes (240 over 192 on N = 2880, 256 on L, D, E).
-// `atoms` is the K atoms one cluster works through in the launch.
-double cycles_per_mma(const Variant &v, int bn, int64_t tiles, int slots, double atoms) {
-    const bool few_waves = v.cg == 2 ? tiles <= 3 * int64_t(slots) : tiles <= slots && atoms <= 64.0;
-    if (few_waves)
-        return 0.4 * bn + (v.cg == 1 && v.atoms < 2 ? 26.0 : 24.0);
-    if (v.cg == 2)
-        return std::max(0.344 * bn + 60.0, 130.0);
-    return v.atoms >= 2 ? 0.344 * bn + 63.0 : std::max(0.396 * bn + 70.0, 150.0);
-}
-
-// Model of one launch in cycles per SM: waves x K-atoms x 4 MMAs x cycles per MMA. Waves count
-// whole, so the model trades tile width against wave quantisation and M/N tail waste. With
-// splits > 1 every tile (hybrid = false), or only tiles % slots of them (hybrid = true: the
-// tiles that would form a partial last wave), is cut into `splits` K ranges whose fp32
-// partials the last arriving split sums. Split units run first; in the hybrid form the whole
-// tiles that follow hide that fix-up, in the plain form it ends the launch.
-double model_cycles(const gg_problem *p, const Variant &v, int bn, int slots, int splits, bool hybrid, int sk = 0) {
-    const int64_t tiles = tiles_for(p, v, bn);
-    const int64_t atoms = (p->k + gg::kBK - 1) / gg::kBK;
-    // A CTA pair pays a fixed start-up cost (cluster barrier, cross-CTA pipeline fill) that only
-    // matters for launches of a few microseconds.
-    double fixed = v.cg == 2 ? 1500.0 : 0.0;
-    double unit_atoms;
-    if (sk > 0) {
-        // stream-K: whole waves, then an equal share of the stream-K region's atoms. Every cluster
-        // writes an fp32 partial and reads one back at about the same time, so the fix-up runs at
-        // the GPU-wide store rate: timestamps inside the kernel show ~3.5-5 us per 128 x 240 fp32
-        // partial per CTA (~16 bytes per cycle per SM) plus ~2 us of fence and arrival latency.
-        const int64_t skt = gg::sk_tiles_for(tiles, slots, atoms, sk);
-        const int64_t S = skt * atoms;
-        unit_atoms = double((tiles - skt) / slots) * double(atoms) + double((S + slots - 1) / slots);
-        fixed += 4000.0 + double(gg::sk_max_pieces(skt, slots, atoms) - 1) * double(bn) * 64.0;
-    } else if (splits <= 1) {
-        unit_atoms = double((tiles + slots - 1) / slots) * double(atoms);
-    } else {
-        const int64_t whole = hybrid ? tiles / slots * slots : 0;
-        const int64_t split_units = (tiles - whole) * splits;
-        unit_atoms = double(whole / slots) * double(atoms) +
-                     double((split_units + slots - 1) / slots) * double((atoms + splits - 1) / splits);
-        // fix-up: each split writes its fp32 partial (128 x bn per CTA), the last arriver reads
-        // the others back and stores out with direct stores
-        fixed += hybrid ? 1000.0 + double(splits - 1) * double(bn) * 12.0 : 2500.0 + double(splits) * double(bn) * 10.0;
-    }
-    return unit_atoms * 4.0 * cycles_per_mma(v, bn, tiles, slots, unit_atoms) + fixed;
-}
-
-// Pick the variant, tile width and split-K / stream-K form with the smallest modelled time.
-// `forced_variant` >= 0 and `forced_bn` > 0 restrict the search; `min_splits`..`max_splits` is
-// the range of split counts tried; `forced_hybrid` is -1 (either form), 0 or 1; `stream_k` is -1
-// (automatic), 0 (never) or the stream-K kind to use. `pairs` is the number of co-resident CTA
-// pairs of the 2-CTA variant.
-Choice choose_tiling(const gg_problem *p, int num_sms, int pairs, int forced_variant, int forced_bn,
-                     int max_splits = 1, bool mn_major_b = false, int min_splits = 1, int forced_hybrid = -1,
-                     int stream_k = 0) {
-    Choice best{-1, 0, 1, false, 0};
-    double best_t = 0;
-    const int64_t atoms = (p->k + gg::kBK - 1) / gg::kBK;
-    for (int vi = 0; vi < 3; ++vi) {
-        if (forced_variant >= 0 && vi != forced_variant)
-            continue;
-        const Variant &v = variant_at(vi);
-        const int slots = v.cg == 2 ? pairs : num_sms;
-        if (slots < 1)
-            continue;
-        for (int bn = v.bn; bn >= 16; bn -= 16) {
-            if (forced_bn > 0 && bn != forced_bn)
-                continue;
-            if (forced_bn <= 0 && bn < 96)
-                continue;  // narrower tiles only on request
-            if (forced_bn <= 0 && bn < 128 && tiles_for(p, v, bn) > slots)
-                continue;  // below 128 columns only for a one-wave tiling (it fills more SMs)
-            // A width in steps of 16 (not 32) only where it tiles N exactly (N = 2880 = 12 x 240
-            // against 256's 6.7% padding: +2-9% measured); with a ragged N tail it measured
-            // between -5% and +3% against the widths in steps of 32.
-            if (forced_bn <= 0 && bn % 32 != 0 && p->n % bn != 0)
-                continue;
-            if (mn_major_b && (bn / v.cg) % 64 != 0)
-                continue;  // MN-major B is loaded in 64-column boxes
-            const int64_t tiles = tiles_for(p, v, bn);
-            // stream-K candidates (kinds 1 and 2), unless split-K is forced
-            for (int kind = 1; kind <= 2 && min_splits == 1 && stream_k != 0; ++kind) {
-                if (stream_k > 0 && kind != stream_k)
-                    continue;
-                const int64_t skt = gg::sk_tiles_for(tiles, slots, atoms, kind);
-                if (skt == 0)
-                    continue;
-                const int pieces = gg::sk_max_pieces(skt, slots, atoms);
-                // automatic: at most 4 pieces per tile and >= 4 atoms per cluster
-                if (stream_k < 0 && (pieces > 4 || skt * atoms < 4 * int64_t(slots)))
-                    continue;
-                const double t = model_cycles(p, v, bn, slots, 1, false, kind);
-                if (best.variant < 0 || t < best_t * 0.999) {
-                    best = {vi, bn, pieces, false, kind};
-                    best_t = t;
-                }
-            }
-            if (stream_k > 0)
-                continue;  // a forced stream-K kind is the only form tried
-            for (int s = min_splits; s <= max_splits; ++s) {
-                for (int hy = 0; hy < 2; ++hy) {
-                    if ((s == 1 && hy == 1) || (forced_hybrid >= 0 && s > 1 && hy != forced_hybrid))
-                        continue;
-                    const bool forced = min_splits > 1;
-                    if (s > 1 && !forced) {
-                        // automatic split-K: >= 8 K atoms per split, and the split units of the
-                        // pure form fill at most 4 waves, those of the hybrid form 2
-                        const int64_t rem = hy ? tiles % slots : tiles;
-                        if (atoms < 8 * s || rem == 0 || (hy && tiles < slots) || (!hy && tiles >= slots) ||
-                            rem * s > (hy ? 2 : 4) * int64_t(slots))
-                            continue;
-                    }
-                    if (s > 1 && hy && tiles % slots == 0)
-                        continue;  // no partial wave to split
-                    const double t = model_cycles(p, v, bn, slots, s, hy == 1);
-                    if (best.variant < 0 || t < best_t * 0.999) {
-                        best = {vi, bn, s, hy == 1, 0};
-                        best_t = t;
-                    }
-                }
-            }
-        }
-    }
-    return best;
-}
-
-
 
 }  // namespace
 
@@ -578,7 +436,7 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     // a forced split count is used exactly (the tiling is chosen for it)
     // stream-K is tried unless split-K is forced (or for wgrad)
     const int stream_k = op == gg::kOpWgrad || h->opt_split > 1 ? 0 : h->opt_stream_k;
-    const Choice ch = choose_tiling(&cm, num_sms, pairs, h->opt_variant, h->opt_bn, max_splits, mn_b,
+    const Choice ch = gg::choose_tiling(tile_shapes(), kNumVariants, &cm, num_sms, pairs, h->opt_variant, h->opt_bn, max_splits, mn_b,
                                     h->opt_split > 1 && op != gg::kOpWgrad ? h->opt_split : 1, h->opt_sk_tail,
                                     stream_k);
     if (ch.variant < 0)
@@ -1028,7 +886,7 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
     }
 
     // ---- variant, group arguments (host stack), descriptors ----
-    const Choice ch = choose_tiling(p, d->num_sms, d->clusters_v0, -1, 0, 1);
+    const Choice ch = gg::choose_tiling(tile_shapes(), kNumVariants, p, d->num_sms, d->clusters_v0, -1, 0, 1);
     if (ch.variant < 0) {
         copy_msg(why, why_len, "no kernel variant fits this device");
         return GG_NOT_SUPPORTED;

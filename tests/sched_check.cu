@@ -12,11 +12,14 @@
 // Then decode_tile, for random group sizes (empty groups included), widths, bands and both raster
 // orders: tile indices map onto every (group, m-tile, n-tile) exactly once.
 // Prints "ok <launches> <units> <tables>" and exits 0, or prints the first violation and exits 1.
+// With `choose B,M,N,K ...` it prints the cost model's automatic choice for each problem instead.
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <string>
 #include <vector>
 
+#include "gg_b200.h"
 #include "gg_kernel.cuh"
 #include "gg_sched.h"
 
@@ -159,7 +162,28 @@ bool check_decode(const std::vector<int64_t> &group_m, int tiles_n, int band, in
 
 }  // namespace
 
+// `choose B,M,N,K ...`: the library's automatic choice for balanced problems on a B200 (148 SMs,
+// 74 CTA pairs), with the split-K range prepare allows (up to 4 unless the fp32 partials of
+// every tile would exceed 512 MB), one line per problem: variant bn splits hybrid stream_k.
+int choose(int argc, char **argv) {
+    const gg::TileShape shapes[3] = {{2, 256, 256, 2}, {1, 256, 128, 1}, {1, 128, 128, 2}};
+    for (int i = 2; i < argc; ++i) {
+        int B = 0;
+        long long M = 0, N = 0, K = 0;
+        if (std::sscanf(argv[i], "%d,%lld,%lld,%lld", &B, &M, &N, &K) != 4)
+            return 2;
+        std::vector<int64_t> gm(size_t(B), M);
+        const gg_problem p{0, B, N, K, gm.data(), nullptr, nullptr, nullptr};
+        const int max_splits = double(B) * double(M) * double(N) * 4.0 * 4 > 512.0 * (1 << 20) ? 1 : 4;
+        const gg::Choice c = gg::choose_tiling(shapes, 3, &p, 148, 74, -1, 0, max_splits, false, 1, -1, 0);
+        std::printf("%d %d %d %d %d\n", c.variant, c.bn, c.splits, c.hybrid ? 1 : 0, c.sk);
+    }
+    return 0;
+}
+
 int main(int argc, char **argv) {
+    if (argc > 1 && std::string(argv[1]) == "choose")
+        return choose(argc, argv);
     const int launches = argc > 1 ? std::atoi(argv[1]) : 20000;
     Rng rng{0x9E3779B97F4A7C15ull};
     long long units = 0;
