@@ -10,12 +10,17 @@ enqueued through the C ABI (gg_run), timed back to back like the reference harne
 (bench/bench_main.cpp:490-501).
 
 Multi-GPU (torchrun, one process per GPU, NCCL only for the barrier and the max-over-ranks
-timing): experts are sharded contiguously (gg_expert_shard); every GPU keeps 8 experts, so the
-job grows with N ("scaling": "weak"). There is no collective on the GEMM path.
+timing): experts are sharded contiguously (gg_expert_shard); every GPU keeps 8 experts of L, so
+the job grows with N ("scaling": "weak"). There is no collective on the GEMM path. Beside it, at
+every N, the same line carries `config_E`: BASELINE configs[4] (256 experts in total) sharded
+over the N GPUs (strong scaling), with rank 0's one-GPU time of the whole problem in the same run
+as the efficiency base, and (with --allgather) an NCCL all-gather of its outputs, timed apart.
+After the timed region a seconds-long back-to-back leg on the headline config reports the
+sustained (power-capped) throughput and SM clock (`sustained`).
 
 `--impl reference` times the reference op's CPU fp32 path (the reference has no CPU
-implementation; the oracle port of its fp32 math runs on all host cores) on a bounded sample
-of the same workload, on rank 0 only.
+implementation; the oracle port of its fp32 math runs on all host cores), one whole expert of
+the workload per step, on rank 0 only.
 """
 from __future__ import annotations
 
@@ -35,7 +40,7 @@ PKG_DIR = os.path.join(ROOT, "groupgemm-cktile-optimized_b200")
 
 METRIC = "grouped-GEMM TFLOPS/GPU (bf16) and % of B200 dense peak; aggregate at 1/2/4/8 GPU"
 DATASHEET_TFLOPS = 2250.0
-FALLBACK = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+FALLBACK = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
 
 CONFIGS = {
     # name: (experts per GPU or total, M, N, K, dtype, sharding)
@@ -43,6 +48,9 @@ CONFIGS = {
               desc="L: B=8 experts per GPU, M=4096, N=4096, K=7168, bf16 (BASELINE configs[1])"),
     "E": dict(b=256, m=512, n=4096, k=7168, dtype="bf16", per_gpu=False,
               desc="E: B=256 experts sharded over the GPUs, M=512, N=4096, K=7168, bf16 (BASELINE configs[4])"),
+    # E's per-GPU share at 8 GPUs on its own (the reduced case for DRAM captures)
+    "E32": dict(b=32, m=512, n=4096, k=7168, dtype="bf16", per_gpu=True,
+                desc="E32: config E's per-GPU share at 8 GPUs, B=32 experts, M=512, N=4096, K=7168, bf16"),
     "D": dict(b=32, m=2048, n=7168, k=2048, dtype="fp16", per_gpu=True,
               desc="D: B=32 experts per GPU, M=2048, N=7168, K=2048, fp16 (BASELINE configs[2])"),
     "P": dict(b=16, m=1000, n=2880, k=2880, dtype="bf16", per_gpu=True,
@@ -72,6 +80,12 @@ def group_sizes(cfg, g0, g1):
     sizes = np.floor(weights / weights.sum() * total).astype(np.int64)
     sizes[np.argmax(sizes)] += total - sizes.sum()
     return [int(v) for v in sizes[g0:g1]]
+
+
+def algorithmic_bytes(group_m, n, k, elem=2):
+    """Each operand read once, the output written once: 2 (sum(M) K + B N K + sum(M) N)."""
+    rows = int(sum(group_m))
+    return int(elem * (rows * k + len(group_m) * n * k + rows * n))
 
 
 def load_package():
@@ -181,21 +195,31 @@ class ClockSampler:
         return out
 
 
+def cpu_expert_rate(cfg, orc, threads, x, w, steps):
+    """Seconds of each of `steps` whole-expert fp32 GEMMs (M x N x K) with the oracle port."""
+    dt = 0 if cfg["dtype"] == "bf16" else 1
+    out = np.zeros((cfg["m"], cfg["n"]), np.float32)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        orc.grouped_gemm_f32(x, w, [cfg["m"]], dt, threads=threads, out=out)
+        times.append(time.perf_counter() - t0)
+    return times
+
+
 def cpu_baseline(cfg, budget_s: float = 20.0):
     """Oracle port of the fp32 reference path on all host cores. Whole experts of the workload
     (M x N x K each) are computed one after another until every expert of one GPU's share is
-    done or `budget_s` has passed; the sample is the experts completed."""
+    done or `budget_s` has passed; the sample is the experts completed. The reference arm
+    (`--impl reference`) times the same unit, one expert per step."""
     orc = load_oracle()
     dt = 0 if cfg["dtype"] == "bf16" else 1
     n, k, m, b = cfg["n"], cfg["k"], cfg["m"], cfg["b"]
     threads = orc.hw_threads()
     x, w = orc.make_inputs([m], n, k, dt)  # one expert's operands, reused per expert
     done, el = 0, 0.0
-    out = np.zeros((m, n), np.float32)
     while done < b and el < budget_s:
-        t0 = time.perf_counter()
-        orc.grouped_gemm_f32(x, w, [m], dt, threads=threads, out=out)
-        el += time.perf_counter() - t0
+        el += cpu_expert_rate(cfg, orc, threads, x, w, 1)[0]
         done += 1
     flops = 2.0 * done * m * n * k
     return {"value": round(flops / el / 1e12, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
@@ -204,6 +228,9 @@ def cpu_baseline(cfg, budget_s: float = 20.0):
 
 
 def run_reference(args, cfg):
+    """The reference arm: the oracle port of the reference op's fp32 math (the reference has no
+    CPU implementation of its own) on all host threads. A step is one whole expert of the
+    workload (M x N x K), the unit `cpu_baseline` times too."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
@@ -212,21 +239,12 @@ def run_reference(args, cfg):
     n, k, m = cfg["n"], cfg["k"], cfg["m"]
     threads = orc.hw_threads()
     x, w = orc.make_inputs([m], n, k, dt)
-    # bounded sample per step: rows of one expert sized for ~1.5 s per step
-    t0 = time.perf_counter()
-    orc.grouped_gemm_f32(x, w, [m], dt, max_rows=16, threads=threads)
-    rows = int(max(16, min(m, 16 * 1.5 / max(time.perf_counter() - t0, 1e-6)))) // 16 * 16 or 16
-    for _ in range(args.warmup):
-        orc.grouped_gemm_f32(x, w, [m], dt, max_rows=rows, threads=threads)
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        orc.grouped_gemm_f32(x, w, [m], dt, max_rows=rows, threads=threads)
-        times.append(time.perf_counter() - t0)
+    cpu_expert_rate(cfg, orc, threads, x, w, args.warmup)
+    times = cpu_expert_rate(cfg, orc, threads, x, w, args.steps)
     el = sum(times)
-    flops = 2.0 * rows * n * k * args.steps
+    flops = 2.0 * m * n * k * args.steps
     value = flops / el / 1e12
-    sample = (f"each step: fp32 GEMM of {rows} rows x N={n} x K={k} of one expert of the {cfg['desc']} workload, "
+    sample = (f"each step: fp32 GEMM of one whole expert ({m} rows x N={n} x K={k}) of the {cfg['desc']} workload, "
               f"oracle port of the reference's fp32 math on {threads} host threads")
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": "TFLOPS", "impl": "reference",
@@ -243,13 +261,55 @@ def run_reference(args, cfg):
 
 
 def load_traffic(cfg_name):
-    """Per-launch DRAM bytes of the kernel from the committed ncu summary (None if absent)."""
+    """ncu DRAM captures of the kernel for a config (profiles/gg_sm100_<cfg>_traffic.json): a list
+    of {bytes_per_launch, algorithmic_bytes, source, ...}, one per captured launch size."""
     path = os.path.join(ROOT, "profiles", f"gg_sm100_{cfg_name}_traffic.json")
     try:
         with open(path) as f:
-            return json.load(f)
+            d = json.load(f)
     except (OSError, ValueError):
-        return None
+        return []
+    caps = d.get("captures", [d]) if isinstance(d, dict) else d
+    return [c for c in caps if c.get("bytes_per_launch")]
+
+
+def launch_traffic(captures, alg_bytes):
+    """DRAM bytes of one launch whose algorithmic bytes are `alg_bytes`, from the captures of the
+    same config: the capture of that size if there is one, else the capture nearest in size with
+    its traffic scaled in proportion to the algorithmic bytes (the re-read factor is taken as
+    size-independent, which the source string says). (None, reason) when nothing applies."""
+    usable = [c for c in captures if c.get("algorithmic_bytes")]
+    if not usable:
+        return None, "no ncu DRAM capture with its algorithmic bytes for this config"
+    best = min(usable, key=lambda c: abs(np.log(c["algorithmic_bytes"] / alg_bytes)))
+    if best["algorithmic_bytes"] == alg_bytes:
+        return int(best["bytes_per_launch"]), best.get("source", "")
+    scaled = int(round(best["bytes_per_launch"] * alg_bytes / best["algorithmic_bytes"]))
+    ratio = best["bytes_per_launch"] / best["algorithmic_bytes"]
+    return scaled, (f"scaled from a capture of {best['algorithmic_bytes'] / 1e9:.3f} GB algorithmic "
+                    f"({ratio:.3f}x traffic/algorithmic) to this launch's {alg_bytes / 1e9:.3f} GB: "
+                    f"{best.get('source', '')}")
+
+
+def roofline(flops, alg_bytes, ms_launch, peaks, peak_src, captures, kernel_detail):
+    """Roofline object of one rank's launch: tensor side against the measured cuBLAS burst, memory
+    side (algorithmic bytes and ncu DRAM traffic, scaled to this launch) against the measured copy
+    bandwidth."""
+    achieved = flops / (ms_launch * 1e-3) / 1e12
+    peak = float(peaks.get("bf16_tflops", FALLBACK["bf16_tflops"]))
+    sustained_peak = float(peaks.get("bf16_tflops_sustained", FALLBACK["bf16_tflops_sustained"]))
+    traffic, tsrc = launch_traffic(captures, alg_bytes)
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK["hbm_gbs"]))
+    alg_gbs = alg_bytes / (ms_launch * 1e-3) / 1e9
+    return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} bf16 burst (cuBLAS)",
+            "frac_of_sustained": round(achieved / sustained_peak, 4),
+            "frac_of_datasheet_2250": round(achieved / DATASHEET_TFLOPS, 4),
+            "traffic": traffic, "traffic_source": tsrc, "algorithmic_bytes": int(alg_bytes),
+            "kernel": "gg::grouped_gemm_sm100 (" + kernel_detail + ")",
+            "hbm": {"algorithmic_gbs": round(alg_gbs, 1), "peak_gbs": hbm_peak,
+                    "frac_algorithmic": round(alg_gbs / hbm_peak, 4),
+                    "traffic_gbs": round(traffic / (ms_launch * 1e-3) / 1e9, 1) if traffic else None}}
 
 
 def run_backward(args, cfg):
@@ -354,6 +414,219 @@ def run_backward(args, cfg):
     return 0 if bad == 0 else 1
 
 
+class Problem:
+    """One rank's share of a config on its GPU: seeded N(0,1) inputs generated on the device, the
+    output buffer and a prepared backend handle."""
+
+    def __init__(self, gg, torch, cfg, g0, g1, seed, stream, variant=-1):
+        self.cfg = cfg
+        self.group_m = group_sizes(cfg, g0, g1)
+        self.rows = sum(self.group_m)
+        n, k = cfg["n"], cfg["k"]
+        tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        self.x = torch.randn(self.rows, k, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
+        self.w = torch.empty(g1 - g0, n, k, device="cuda", dtype=tdt)
+        for g in range(g1 - g0):  # per expert to bound the fp32 temporary
+            self.w[g] = torch.randn(n, k, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
+        self.out = torch.empty(self.rows, n, device="cuda", dtype=tdt)
+        self.flops = 2.0 * self.rows * n * k
+        self.alg_bytes = algorithmic_bytes(self.group_m, n, k)
+        self.backend = gg.make_b200_backend()
+        if variant >= 0:
+            self.backend.set_option("variant", variant)
+        why = self.backend.prepare(gg.DTYPES[cfg["dtype"]], self.group_m, n, k, self.x.data_ptr(),
+                                   self.w.data_ptr(), self.out.data_ptr(), stream.cuda_stream)
+        if why:
+            raise SystemExit(f"prepare refused the workload: {why}")
+
+    def release(self):
+        self.backend.release()
+        del self.x, self.w, self.out
+
+
+def time_launches(torch, prob, stream, steps, warmup, dist=None, sampler=None):
+    """Mean device time (ms) of `steps` back-to-back launches after `warmup` untimed ones, CUDA
+    events on the launching stream, barrier + synchronize on both sides. Returns (this rank's ms,
+    max over ranks)."""
+    s = stream.cuda_stream
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            prob.backend.run(s)
+    torch.cuda.synchronize()
+    if prob.backend.device_status(s) != 0:
+        raise SystemExit("kernel reported a bounded-wait timeout during warm-up")
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.__enter__()
+    try:
+        ev0.record(stream)
+        for _ in range(steps):
+            prob.backend.run(s)
+        ev1.record(stream)
+        ev1.synchronize()
+    finally:
+        if sampler:
+            sampler.__exit__()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    if prob.backend.device_status(s) != 0:
+        raise SystemExit("kernel reported a bounded-wait timeout in a timed region")
+    ms = ev0.elapsed_time(ev1) / steps
+    return ms, max_over_ranks(torch, dist, ms)
+
+
+def max_over_ranks(torch, dist, v):
+    if not dist:
+        return v
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sustained_leg(torch, prob, stream, dist, local_rank, seconds, peaks):
+    """Back-to-back launches for about `seconds` after the timed region: the throughput and SM
+    clock the kernel holds once the board sits at its power cap."""
+    s = stream.cuda_stream
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    prob.backend.run(s)
+    ev1.record(stream)
+    ev1.synchronize()
+    launches = max(10, int(seconds * 1e3 / max(ev0.elapsed_time(ev1), 1e-3)))
+    launches = int(max_over_ranks(torch, dist, launches))  # every rank runs the same count
+    sampler = ClockSampler(local_rank)
+    ms_rank, ms = time_launches(torch, prob, stream, launches, 0, dist, sampler)
+    tflops = prob.flops / (ms_rank * 1e-3) / 1e12
+    clk = sampler.summary()
+    out = {"tflops_per_gpu": round(prob.flops / (ms * 1e-3) / 1e12, 2), "launches": launches,
+           "seconds": round(ms * launches / 1e3, 2), "ms_per_launch": round(ms, 4),
+           "median_sm_mhz": clk.get("sm_mhz"), "reasons": clk.get("reasons"),
+           "power_w_median": clk.get("power_w_median"),
+           "frac_of_sustained_peak": round(tflops / float(peaks.get("bf16_tflops_sustained",
+                                                                    FALLBACK["bf16_tflops_sustained"])), 4),
+           "frac_of_datasheet_2250": round(tflops / DATASHEET_TFLOPS, 4)}
+    if clk.get("sm_mhz"):
+        out["tflops_per_ghz"] = round(tflops / (clk["sm_mhz"] / 1e3), 1)
+    return out
+
+
+def config_e_leg(torch, gg, dist, world, rank, local_rank, stream, steps, warmup, allgather, peaks, peak_src):
+    """BASELINE configs[4] (256 experts) sharded contiguously over the `world` GPUs: aggregate
+    TFLOPS at max-over-ranks time, per-GPU TFLOPS, and the efficiency against rank 0's one-GPU
+    time of the whole problem measured in the same run (the other ranks wait meanwhile)."""
+    cfg = CONFIGS["E"]
+    total_flops = 2.0 * sum(group_sizes(cfg, 0, cfg["b"])) * cfg["n"] * cfg["k"]
+    ms_one = None
+    if world > 1:
+        if rank == 0:
+            whole = Problem(gg, torch, cfg, 0, cfg["b"], 2000, stream)
+            ms_one, _ = time_launches(torch, whole, stream, steps, warmup, None, ClockSampler(local_rank))
+            whole.release()
+            del whole
+            torch.cuda.empty_cache()
+        dist.barrier()
+    g0, g1 = gg.expert_shard(cfg["b"], world, rank)
+    prob = Problem(gg, torch, cfg, g0, g1, 2000 + rank, stream)
+    clocks = ClockSampler(local_rank)
+    ms_rank, ms = time_launches(torch, prob, stream, steps, warmup, dist, clocks)
+    if world == 1:
+        ms_one = ms
+    agg = total_flops / (ms * 1e-3) / 1e12
+    one = total_flops / (ms_one * 1e-3) / 1e12 if ms_one else None
+    res = {"workload": cfg["desc"], "scaling": "strong", "experts": cfg["b"], "n_gpus": world,
+           "tflops": round(agg, 2), "tflops_per_gpu": round(agg / world, 2), "ms_per_step": round(ms, 4),
+           "steps": steps, "ranges": [list(gg.expert_shard(cfg["b"], world, r)) for r in range(world)],
+           "tflops_1gpu_same_run": round(one, 2) if one else None,
+           "efficiency_vs_1gpu": round(agg / (world * one), 4) if one else None,
+           "rank0_clocks": clocks.summary(),
+           "rank0_roofline": roofline(prob.flops, prob.alg_bytes, ms_rank, peaks, peak_src, load_traffic("E"),
+                                      prob.backend.detail())}
+    if allgather and dist:
+        gathered = torch.empty(world * prob.rows, cfg["n"], device="cuda", dtype=prob.out.dtype)
+        for _ in range(2):
+            dist.all_gather_into_tensor(gathered, prob.out)
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(5):
+            dist.all_gather_into_tensor(gathered, prob.out)
+        a1.record()
+        a1.synchronize()
+        res["allgather"] = {"ms": round(max_over_ranks(torch, dist, a0.elapsed_time(a1) / 5), 4),
+                            "bytes_per_rank": prob.rows * cfg["n"] * 2, "how": "NCCL all_gather_into_tensor"}
+        del gathered
+    prob.release()
+    del prob
+    torch.cuda.empty_cache()
+    return res
+
+
+def e2e_leg(torch, gg, prob, stream, dist, steps, variant):
+    """End to end through the C ABI with host buffers: every step copies its x and w from pinned
+    host memory and its output back. Two device buffer sets (each with its own prepared handle)
+    let step i+1's host->device copies run on a copy stream while step i computes and copies
+    back, as a serving loop would."""
+    s = stream.cuda_stream
+    x, w, out = prob.x, prob.w, prob.out
+    cfg = prob.cfg
+    hx = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+    hw = torch.empty(w.shape, dtype=w.dtype, pin_memory=True)
+    ho = [torch.empty(out.shape, dtype=out.dtype, pin_memory=True) for _ in range(2)]
+    hx.copy_(x)
+    hw.copy_(w)
+    sets = [(x, w, out, prob.backend)]
+    x2, w2, out2 = torch.empty_like(x), torch.empty_like(w), torch.empty_like(out)
+    b2 = gg.make_b200_backend()
+    if variant >= 0:
+        b2.set_option("variant", variant)
+    if b2.prepare(gg.DTYPES[cfg["dtype"]], prob.group_m, cfg["n"], cfg["k"], x2.data_ptr(), w2.data_ptr(),
+                  out2.data_ptr(), s):
+        raise SystemExit("prepare refused the second buffer set")
+    sets.append((x2, w2, out2, b2))
+    copy_stream = torch.cuda.Stream()
+    copied = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+    torch.cuda.synchronize()
+
+    def e2e_step(i):
+        xd, wd, od, be = sets[i % 2]
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(done[i % 2])  # the set's previous step has finished with it
+            xd.copy_(hx, non_blocking=True)
+            wd.copy_(hw, non_blocking=True)
+            copied[i % 2].record(copy_stream)
+        with torch.cuda.stream(stream):
+            stream.wait_event(copied[i % 2])
+            be.run(s)
+            ho[i % 2].copy_(od, non_blocking=True)
+            done[i % 2].record(stream)
+
+    for i in range(2):  # warm-up of both sets
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(copy_stream)
+    for i in range(steps):
+        e2e_step(i)
+    ev1.record(stream)
+    ev1.synchronize()
+    e2e_ms = ev0.elapsed_time(ev1) / steps
+    for _, _, _, be in sets:
+        if be.device_status(s) != 0:
+            raise SystemExit("kernel reported a bounded-wait timeout in the end-to-end steps")
+    b2.release()
+    del x2, w2, out2
+    return max_over_ranks(torch, dist, e2e_ms), int(hx.numel() * 2 + hw.numel() * 2), int(ho[0].numel() * 2)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -362,8 +635,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="L", choices=sorted(CONFIGS))
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--sustained-s", type=float, default=2.5,
+                    help="seconds of the back-to-back sustained leg after the timed region (0 = skip)")
+    ap.add_argument("--no-config-e", action="store_true", help="skip the config E strong-scaling leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--allgather", action="store_true", help="also time an NCCL all-gather of the outputs")
+    ap.add_argument("--allgather", action="store_true",
+                    help="also time an NCCL all-gather of config E's sharded outputs")
     ap.add_argument("--variant", type=int, default=-1)
     ap.add_argument("--op", default="forward", choices=["forward", "dgrad", "wgrad"],
                     help="dgrad/wgrad: time a backward grouped GEMM on one GPU (not the headline line)")
@@ -393,193 +670,70 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     gg = load_package()
-    dtype = gg.DTYPES[cfg["dtype"]]
-    tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
+    peaks, peak_src = measured_peaks()
     total_groups, (g0, g1) = shard_of(cfg, world, rank, gg)
-    ng = g1 - g0
-    m, n, k = cfg["m"], cfg["n"], cfg["k"]
-    group_m = group_sizes(cfg, g0, g1)
-    rows = sum(group_m)
-    gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
-    x = torch.randn(rows, k, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
-    w = torch.empty(ng, n, k, device="cuda", dtype=tdt)
-    for g in range(ng):  # per expert to bound the fp32 temporary
-        w[g] = torch.randn(n, k, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
-    out = torch.empty(rows, n, device="cuda", dtype=tdt)
     stream = torch.cuda.Stream()
-    s = stream.cuda_stream
-    backend = gg.make_b200_backend()
-    if args.variant >= 0:
-        backend.set_option("variant", args.variant)
-    why = backend.prepare(dtype, group_m, n, k, x.data_ptr(), w.data_ptr(), out.data_ptr(), s)
-    if why:
-        raise SystemExit(f"prepare refused the workload: {why}")
-    flops_rank = 2.0 * rows * n * k
+    prob = Problem(gg, torch, cfg, g0, g1, 1000 + rank, stream, args.variant)
+    n, k = cfg["n"], cfg["k"]
 
     # ---- device-timed steps (inputs resident in HBM) ----
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            backend.run(s)
-    torch.cuda.synchronize()
-    if backend.device_status(s) != 0:
-        raise SystemExit("kernel reported a bounded-wait timeout during warm-up")
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local_rank) as clocks:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            backend.run(s)
-        ev1.record(stream)
-        ev1.synchronize()
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    ms_total = ev0.elapsed_time(ev1)
-    if backend.device_status(s) != 0:
-        raise SystemExit("kernel reported a bounded-wait timeout in the timed region")
-    ms_step_rank = ms_total / args.steps
-    if dist:
-        t = torch.tensor([ms_step_rank], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_step = float(t.item())
-    else:
-        ms_step = ms_step_rank
+    clocks = ClockSampler(local_rank)
+    ms_step_rank, ms_step = time_launches(torch, prob, stream, args.steps, args.warmup, dist, clocks)
     total_flops = 2.0 * sum(group_sizes(cfg, 0, total_groups)) * n * k
     value = total_flops / (ms_step * 1e-3) / 1e12
-
-    # ---- optional all-gather of the expert outputs (timed separately, not in value) ----
-    allgather = None
-    if args.allgather and dist:
-        gathered = torch.empty(world * rows, n, device="cuda", dtype=tdt)
-        for _ in range(2):
-            dist.all_gather_into_tensor(gathered, out)
-        torch.cuda.synchronize()
-        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a0.record()
-        for _ in range(5):
-            dist.all_gather_into_tensor(gathered, out)
-        a1.record()
-        a1.synchronize()
-        t = torch.tensor([a0.elapsed_time(a1) / 5], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        allgather = {"ms": round(float(t.item()), 4), "bytes_per_rank": rows * n * 2}
-        del gathered
+    detail = prob.backend.detail()
+    roof = roofline(prob.flops, prob.alg_bytes, ms_step_rank, peaks, peak_src, load_traffic(args.config), detail)
 
     # ---- end to end through the C ABI with host buffers ----
-    # Every step copies its x and w from pinned host memory and its output back. Two device
-    # buffer sets (each with its own prepared handle) let step i+1's host->device copies run on
-    # a copy stream while step i computes and copies back, as a serving loop would.
-    hx = torch.empty(x.shape, dtype=tdt, pin_memory=True)
-    hw = torch.empty(w.shape, dtype=tdt, pin_memory=True)
-    ho = [torch.empty(out.shape, dtype=tdt, pin_memory=True) for _ in range(2)]
-    hx.copy_(x)
-    hw.copy_(w)
-    sets = [(x, w, out, backend)]
-    x2, w2, out2 = torch.empty_like(x), torch.empty_like(w), torch.empty_like(out)
-    b2 = gg.make_b200_backend()
-    if args.variant >= 0:
-        b2.set_option("variant", args.variant)
-    if b2.prepare(dtype, group_m, n, k, x2.data_ptr(), w2.data_ptr(), out2.data_ptr(), s):
-        raise SystemExit("prepare refused the second buffer set")
-    sets.append((x2, w2, out2, b2))
-    copy_stream = torch.cuda.Stream()
-    copied = [torch.cuda.Event() for _ in range(2)]
-    done = [torch.cuda.Event() for _ in range(2)]
-    torch.cuda.synchronize()
-    e2e_steps = max(1, min(args.e2e_steps, args.steps))
-
-    def e2e_step(i):
-        xd, wd, od, be = sets[i % 2]
-        with torch.cuda.stream(copy_stream):
-            copy_stream.wait_event(done[i % 2])  # the set's previous step has finished with it
-            xd.copy_(hx, non_blocking=True)
-            wd.copy_(hw, non_blocking=True)
-            copied[i % 2].record(copy_stream)
-        with torch.cuda.stream(stream):
-            stream.wait_event(copied[i % 2])
-            be.run(s)
-            ho[i % 2].copy_(od, non_blocking=True)
-            done[i % 2].record(stream)
-
-    for i in range(2):  # warm-up of both sets
-        e2e_step(i)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0.record(copy_stream)
-    for i in range(e2e_steps):
-        e2e_step(i)
-    ev1.record(stream)
-    ev1.synchronize()
-    e2e_ms = ev0.elapsed_time(ev1) / e2e_steps
-    for _, _, _, be in sets:
-        if be.device_status(s) != 0:
-            raise SystemExit("kernel reported a bounded-wait timeout in the end-to-end steps")
-    b2.release()
-    del x2, w2, out2
-    if dist:
-        t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms, h2d, d2h = e2e_leg(torch, gg, prob, stream, dist, max(1, min(args.e2e_steps, args.steps)), args.variant)
     e2e = {"value": round(total_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
-           "h2d_bytes_per_step": int(hx.numel() * 2 + hw.numel() * 2), "d2h_bytes_per_step": int(ho[0].numel() * 2),
-           "ms_per_step": round(e2e_ms, 3), "steps": e2e_steps,
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
+           "steps": max(1, min(args.e2e_steps, args.steps)),
            "path": "per step: pinned host x,w -> device, gg_run, out -> pinned host; two buffer sets so the "
                    "next step's copies overlap this step's GEMM"}
+
+    # ---- config E sharded over the GPUs, strong scaling ----
+    config_e = None
+    if not args.no_config_e and args.config != "E":
+        config_e = config_e_leg(torch, gg, dist, world, rank, local_rank, stream, min(args.steps, 20), args.warmup,
+                                args.allgather, peaks, peak_src)
+
+    # ---- sustained: seconds of back-to-back launches at the power cap (not in value); last, so
+    # the power-capped state it ends in does not reach the other legs ----
+    sustained = None
+    if args.sustained_s > 0:
+        sustained = sustained_leg(torch, prob, stream, dist, local_rank, args.sustained_s, peaks)
+    prob.release()
+    del prob
+    torch.cuda.empty_cache()
 
     if dist:
         dist.barrier()
     if rank != 0:
-        backend.release()
         if dist:
             dist.destroy_process_group()
         return 0
 
-    peaks, peak_src = measured_peaks()
-    achieved = flops_rank / (ms_step_rank * 1e-3) / 1e12
-    peak = float(peaks.get("bf16_tflops", FALLBACK["bf16_tflops"]))
-    traffic = load_traffic(args.config)
-    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} bf16 burst (cuBLAS)",
-                "frac_of_sustained": round(achieved / float(peaks.get("bf16_tflops_sustained", peak)), 4),
-                "frac_of_datasheet_2250": round(achieved / DATASHEET_TFLOPS, 4),
-                "traffic": traffic.get("bytes_per_launch") if traffic else None,
-                "algorithmic_bytes": int(2 * (rows * k + ng * n * k + rows * n)),
-                "kernel": "gg::grouped_gemm_sm100 (" + backend.detail() + ")"}
-    if traffic:
-        roofline["traffic_source"] = traffic.get("source")
-    # the memory side of the same launch: algorithmic bytes (and measured DRAM traffic, where a
-    # capture exists) per launch time against the measured copy bandwidth
-    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK["hbm_gbs"]))
-    alg_gbs = roofline["algorithmic_bytes"] / (ms_step_rank * 1e-3) / 1e9
-    roofline["hbm"] = {"algorithmic_gbs": round(alg_gbs, 1), "peak_gbs": hbm_peak,
-                       "frac_algorithmic": round(alg_gbs / hbm_peak, 4),
-                       "traffic_gbs": round(traffic["bytes_per_launch"] / (ms_step_rank * 1e-3) / 1e9, 1)
-                       if traffic else None}
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak"
         if cfg["per_gpu"] else "strong",
         "vs_baseline": None, "dtype": cfg["dtype"],
         "data": "synthetic N(0,1) (torch generator on the device), bf16; random expert weights",
-        "config": {"workload": cfg["desc"], "global_batch": total_groups * m, "experts": total_groups,
+        "config": {"workload": cfg["desc"], "global_batch": total_groups * cfg["m"], "experts": total_groups,
                    "parallelism": f"ep{world}", "l2": "inputs larger than L2 (no flush)",
                    "per_gpu_tflops": round(value / world, 2),
                    "pct_of_datasheet_dense_peak": round(100 * value / world / DATASHEET_TFLOPS, 2)},
-        "roofline": roofline,
+        "roofline": roof,
         "e2e": e2e,
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
-        "detail": backend.detail(),
+        "detail": detail,
     }
-    if allgather:
-        line["allgather"] = allgather
-    backend.release()
-    del x, w, out
-    torch.cuda.empty_cache()
+    if sustained:
+        line["sustained"] = sustained
+    if config_e:
+        line["config_E"] = config_e
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg)
     print(json.dumps(line), flush=True)

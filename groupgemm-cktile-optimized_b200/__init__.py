@@ -204,8 +204,10 @@ def run_noalloc(dtype: int, group_m: Sequence[int], n: int, k: int, x_ptr: int, 
 
     The library keeps its small per-call scratch (group offsets and status word, at most 1024
     groups) in a fixed device array instead of allocating it, so nothing is allocated here.
-    Returns (return code, reason or error text, kernel status when `wait`, else 0). Calls that
-    can overlap on the GPU share that array and race; calls in order on one stream are fine."""
+    Returns (return code, reason or error text, status word when `wait`, else 0). The status
+    word is shared and sticky: a waited call reports (and clears) the first bounded-wait timeout
+    of any call since the last waited one. Calls that can overlap on the GPU share that array and
+    race; calls in order on one stream are fine."""
     lib = load_library()
     gm = (ctypes.c_int64 * len(group_m))(*[int(m) for m in group_m])
     prob = GGProblem(int(dtype), len(group_m), int(n), int(k), gm, ctypes.c_void_p(x_ptr or None),

@@ -747,6 +747,21 @@ constexpr size_t kNoAllocScratchBytes = kNoAllocHeader + 2 * (kNoAllocMaxGroups 
 // cudaGetSymbolAddress (see noalloc_device_setup).
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+// The group offsets of one call travel to the device as a kernel parameter (a by-value copy
+// taken when the launch is enqueued, up to 32 KB on CUDA 12.1+ drivers), and a one-block kernel
+// writes them into the scratch array in stream order. So the host neither waits for the stream
+// (as a copy from pageable memory would) nor leaves a pointer to its stack behind.
+struct NoAllocOffsets {
+    int32_t count;                              // entries used: 2 (G + 1)
+    int32_t v[2 * (kNoAllocMaxGroups + 1)];     // tile_off[G+1] then row_off[G+1]
+};
+static_assert(sizeof(NoAllocOffsets) < 32000, "kernel parameter limit");
+
+__global__ void noalloc_publish_offsets(const __grid_constant__ NoAllocOffsets a, int32_t *dst) {
+    for (int i = int(threadIdx.x); i < a.count; i += int(blockDim.x))
+        dst[i] = a.v[i];
+}
+
 constexpr int kNoAllocMaxDevices = 64;
 
 struct NoAllocDevice {
@@ -895,7 +910,9 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
     const int bn = ch.bn;
     const int G = p->group_num;
     const int64_t tiles_n = (p->n + bn - 1) / bn;
-    int32_t meta[2 * (kNoAllocMaxGroups + 1)];
+    NoAllocOffsets offs;
+    offs.count = 2 * (G + 1);
+    int32_t *meta = offs.v;
     int64_t tiles = 0, rows = 0;
     for (int g = 0; g < G; ++g) {
         meta[g] = int32_t(tiles);
@@ -914,13 +931,12 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
 
     uint32_t *d_status = reinterpret_cast<uint32_t *>(d->scratch);
     int32_t *d_meta = reinterpret_cast<int32_t *>(d->scratch + kNoAllocHeader);
-    // The previous call's status and offsets are still in the array: clear the status word and
-    // overwrite the offsets, in stream order behind any earlier call on the same stream.
-    if ((e = cudaMemsetAsync(d_status, 0, sizeof(uint32_t), stream)) != cudaSuccess)
-        return cuda_fail("cudaMemsetAsync(status)", e);
-    if ((e = cudaMemcpyAsync(d_meta, meta, size_t(2 * (G + 1)) * sizeof(int32_t), cudaMemcpyHostToDevice,
-                             stream)) != cudaSuccess)
-        return cuda_fail("cudaMemcpyAsync(group offsets)", e);
+    // The previous call's offsets are still in the array: overwrite them, in stream order behind
+    // any earlier call on the same stream. The status word is left alone: a timeout of an earlier
+    // call stays recorded until a call with status_out reads and clears it.
+    noalloc_publish_offsets<<<1, 256, 0, stream>>>(offs, d_meta);
+    if ((e = cudaGetLastError()) != cudaSuccess)
+        return cuda_fail("group-offset publish launch", e);
 
     const CUtensorMapDataType dt =
         p->dtype == GG_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -977,13 +993,17 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
         return cuda_fail("kernel launch", e);
 
     if (status_out) {
+        // Wait for this call's kernel, then read the shared status word: the first timeout of any
+        // call on this device since the last read. Clear it once reported.
         uint32_t st = 0;
-        if ((e = cudaMemcpyAsync(&st, d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream)) != cudaSuccess)
-            return cuda_fail("cudaMemcpyAsync(status)", e);
         if ((e = cudaStreamSynchronize(stream)) != cudaSuccess)
             return cuda_fail("cudaStreamSynchronize", e);
+        if ((e = cudaMemcpy(&st, d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost)) != cudaSuccess)
+            return cuda_fail("cudaMemcpy(status)", e);
         *status_out = st;
         if (st != 0) {
+            if ((e = cudaMemset(d_status, 0, sizeof(uint32_t))) != cudaSuccess)
+                return cuda_fail("cudaMemset(status)", e);
             std::snprintf(msg, sizeof(msg), "kernel bounded wait timed out: status 0x%x", st);
             copy_msg(why, why_len, msg);
             return GG_ERR_DEVICE;

@@ -180,9 +180,16 @@ int gg_abi_version(void);
  * inside the library (about 8 KB, held by every GPU that loads the library until the process
  * exits), so group_num is limited to 1024; larger problems are refused with GG_NOT_SUPPORTED and
  * a reason in `why`. Nothing is allocated, neither device memory nor host heap memory.
- * Enqueues on `stream` and returns without waiting, unless `status_out` is non-NULL: then it
- * waits for the kernel and stores its status word there (0 = every bounded wait finished;
- * GG_ERR_DEVICE is returned otherwise).
+ * Enqueues two kernels on `stream` (one writes the call's group offsets into the array, passed
+ * by value as its launch parameter; then the grouped GEMM) and returns without waiting for the
+ * GPU, unless `status_out` is non-NULL: then it waits for the stream and stores the status word
+ * there (0 = every bounded wait finished; GG_ERR_DEVICE is returned otherwise).
+ *
+ * The status word is shared by every call on the device and is sticky: a bounded-wait timeout
+ * in any call stays recorded (and makes the waits of later calls give up early, leaving their
+ * output incomplete) until a call with a non-NULL `status_out` reports it and clears it. A call
+ * with `status_out == NULL` therefore reports nothing itself; a caller that never passes
+ * `status_out` cannot detect a timeout.
  *
  * The first call on each device does a one-time set-up (it looks up the array's device address
  * and the kernels' launch limits); make that first call before any stream capture. Every call

@@ -18,7 +18,10 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "lib")
 REF_OUT = os.path.join(HERE, "_ref")
-REFERENCE = os.environ.get("GG_REFERENCE_ROOT", "/root/reference")
+# The reference project's source tree: $GG_REFERENCE_ROOT, else a directory named `reference`
+# beside this repository's root. Where neither exists the reference harness is not built.
+REFERENCE = os.environ.get("GG_REFERENCE_ROOT") or os.path.join(
+    os.path.dirname(os.path.dirname(HERE)), "reference")
 
 
 def _stale(out: str, deps: list[str]) -> bool:

@@ -65,3 +65,65 @@ def test_skewed_routing_is_seeded_complete_and_shard_consistent():
         assert parts == whole
     balanced = bench.CONFIGS["E"]
     assert bench.group_sizes(balanced, 3, 7) == [balanced["m"]] * 4
+
+
+def test_roofline_traffic_follows_the_shard_and_stays_under_hbm_peak():
+    """The DRAM traffic a rank's roofline reports is its own launch's: a capture of the same size
+    is used as is, another size is scaled by the algorithmic bytes, so the traffic rate of a
+    shard never reads above the measured copy bandwidth (a shard's launch time shrinks with its
+    bytes). Launch times here come from a fixed per-GPU rate (1400 TFLOPS), as a bench would see."""
+    bench = _bench()
+    peaks = {"bf16_tflops": 1690.7, "bf16_tflops_sustained": 1409.9, "hbm_gbs": 6540.8}
+    for name in ("E", "L"):
+        cfg = bench.CONFIGS[name]
+        caps = bench.load_traffic(name)
+        assert caps and all(c["algorithmic_bytes"] > 0 for c in caps), name
+        for world in (1, 2, 4, 8):
+            total = cfg["b"] * world if cfg["per_gpu"] else cfg["b"]
+            for rank in (0, world - 1):
+                g0, g1 = rank * total // world, (rank + 1) * total // world
+                gm = bench.group_sizes(cfg, g0, g1)
+                alg = bench.algorithmic_bytes(gm, cfg["n"], cfg["k"])
+                flops = 2.0 * sum(gm) * cfg["n"] * cfg["k"]
+                ms = flops / 1400e12 * 1e3
+                r = bench.roofline(flops, alg, ms, peaks, "measured", caps, "test")
+                assert r["traffic"] is not None and r["traffic"] >= 0.99 * alg, (name, world, r)
+                assert r["hbm"]["traffic_gbs"] < r["hbm"]["peak_gbs"], (name, world, r["hbm"])
+                if world > 1 and name == "E":
+                    assert "scaled" in r["traffic_source"]
+    # no capture: null traffic with a reason, never a number from another launch
+    r = bench.roofline(1e12, 1e9, 1.0, peaks, "measured", [], "test")
+    assert r["traffic"] is None and r["hbm"]["traffic_gbs"] is None and r["traffic_source"]
+
+
+def test_reference_arm_and_cpu_baseline_time_the_same_unit(monkeypatch):
+    """Both CPU figures are whole experts of the workload on all host threads (one expert per
+    step in the reference arm), so they measure the same thing."""
+    bench = _bench()
+    calls = []
+
+    class FakeOracle:
+        @staticmethod
+        def hw_threads():
+            return 4
+
+        @staticmethod
+        def make_inputs(group_m, n, k, dt):
+            return None, None
+
+        @staticmethod
+        def grouped_gemm_f32(x, w, group_m, dt, threads=0, out=None, **kw):
+            calls.append((tuple(group_m), kw.get("max_rows", -1), None if out is None else out.shape))
+
+    monkeypatch.setattr(bench, "load_oracle", lambda: FakeOracle)
+    cfg = dict(bench.CONFIGS["L"], m=64, n=32, k=16)
+    bench.cpu_baseline(cfg, budget_s=60)
+    base_calls, calls[:] = list(calls), []
+
+    class Args:
+        steps, warmup, gpus = 2, 3, 1
+
+    monkeypatch.setenv("RANK", "0")
+    bench.run_reference(Args, cfg)
+    assert base_calls and calls and set(base_calls) == set(calls) == {((64,), -1, (64, 32))}
+    assert len(calls) == Args.steps + Args.warmup

@@ -4,7 +4,7 @@ Such callers (an engine whose memory pool already owns the GPU's memory, a plugi
 fixed budget, a path that must not call cudaMalloc because it can synchronise the device) get
 the grouped GEMM with the library's scratch held in a fixed device array instead of allocated
 buffers. These tests call it through the C ABI and check it against the regular
-gg_prepare/gg_run path on two calls in a row, with the reference's pass rule
+gg_prepare/gg_run path on calls in a row, with the reference's pass rule
 |got - ref| <= 1e-2 + 1e-2 * |ref|. This file is named so that pytest collects it last.
 """
 import numpy as np
@@ -45,7 +45,14 @@ def _close(orc, got_bits, want_bits, dtype):
     return orc.check(got, want)
 
 
-def test_noalloc_matches_regular_path_on_two_calls(gg, orc):
+def _poisoned(torch, elems):
+    return torch.full((elems,), 0x7E5A, dtype=torch.int16, device="cuda")
+
+
+def test_noalloc_back_to_back_calls_match_regular_path(gg, orc):
+    """Two different problems queued back to back on one stream without waiting (the second call
+    overwrites the shared offsets while the first may still be queued), then a waited call whose
+    status covers all three kernels; every output is checked."""
     torch = _torch()
     s = torch.cuda.current_stream().cuda_stream
     cases = [
@@ -56,18 +63,21 @@ def test_noalloc_matches_regular_path_on_two_calls(gg, orc):
     for group_m, n, k, dtype in cases:
         xd, wd = _inputs(torch, orc, group_m, n, k, dtype)
         want = _regular(gg, torch, group_m, n, k, dtype, xd, wd)
-        out = torch.full((sum(group_m) * n,), 0x7E5A, dtype=torch.int16, device="cuda")
-        prepared.append((group_m, n, k, dtype, xd, wd, out, want))
-    # two calls in a row on one stream, then check both outputs
-    for group_m, n, k, dtype, xd, wd, out, _ in prepared:
-        rc, why, st = gg.run_noalloc(dtype, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s,
-                                     wait=True)
-        assert rc == gg.GG_OK and st == 0, (rc, why, st)
+        prepared.append((group_m, n, k, dtype, xd, wd, _poisoned(torch, sum(group_m) * n), want))
     torch.cuda.synchronize()
-    for group_m, n, k, dtype, xd, wd, out, want in prepared:
-        got = out.cpu().numpy().view(np.uint16)
-        bad, mx = _close(orc, got, want, dtype)
-        assert bad == 0, (group_m, bad, mx)
+    for group_m, n, k, dtype, xd, wd, out, _ in prepared:
+        rc, why, st = gg.run_noalloc(dtype, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s)
+        assert rc == gg.GG_OK and st == 0, (rc, why, st)
+    group_m, n, k, dtype, xd, wd, _, want0 = prepared[0]
+    again = _poisoned(torch, sum(group_m) * n)
+    rc, why, st = gg.run_noalloc(dtype, group_m, n, k, xd.data_ptr(), wd.data_ptr(), again.data_ptr(), s,
+                                 wait=True)
+    assert rc == gg.GG_OK and st == 0, (rc, why, hex(st))
+    torch.cuda.synchronize()
+    outputs = [(p[6], p[7], p[3], p[0]) for p in prepared] + [(again, want0, dtype, group_m)]
+    for out, want, dt, gm in outputs:
+        bad, mx = _close(orc, out.cpu().numpy().view(np.uint16), want, dt)
+        assert bad == 0, (gm, bad, mx)
 
 
 def test_noalloc_repeated_call_without_waiting(gg, orc):
@@ -76,13 +86,15 @@ def test_noalloc_repeated_call_without_waiting(gg, orc):
     group_m, n, k = [1000] * 3, 2880, 2880
     xd, wd = _inputs(torch, orc, group_m, n, k, gg.BF16)
     want = _regular(gg, torch, group_m, n, k, gg.BF16, xd, wd)
-    out = torch.zeros(sum(group_m) * n, dtype=torch.int16, device="cuda")
-    for _ in range(2):
-        rc, why, _ = gg.run_noalloc(gg.BF16, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s)
-        assert rc == gg.GG_OK, why
+    outs = [_poisoned(torch, sum(group_m) * n) for _ in range(2)]
+    for i, out in enumerate(outs):
+        rc, why, st = gg.run_noalloc(gg.BF16, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s,
+                                     wait=i == len(outs) - 1)
+        assert rc == gg.GG_OK and st == 0, (rc, why, hex(st))
     torch.cuda.synchronize()
-    bad, mx = _close(orc, out.cpu().numpy().view(np.uint16), want, gg.BF16)
-    assert bad == 0, (bad, mx)
+    for out in outs:
+        bad, mx = _close(orc, out.cpu().numpy().view(np.uint16), want, gg.BF16)
+        assert bad == 0, (bad, mx)
 
 
 def test_noalloc_refuses_more_groups_than_its_scratch_holds(gg):
