@@ -418,7 +418,7 @@ class Problem:
     """One rank's share of a config on its GPU: seeded N(0,1) inputs generated on the device, the
     output buffer and a prepared backend handle."""
 
-    def __init__(self, gg, torch, cfg, g0, g1, seed, stream, variant=-1):
+    def __init__(self, gg, torch, cfg, g0, g1, seed, stream, variant=-1, opts=()):
         self.cfg = cfg
         self.group_m = group_sizes(cfg, g0, g1)
         self.rows = sum(self.group_m)
@@ -433,8 +433,10 @@ class Problem:
         self.flops = 2.0 * self.rows * n * k
         self.alg_bytes = algorithmic_bytes(self.group_m, n, k)
         self.backend = gg.make_b200_backend()
-        if variant >= 0:
-            self.backend.set_option("variant", variant)
+        self.opts = [("variant", variant)] if variant >= 0 else []
+        self.opts += list(opts)
+        for key, val in self.opts:
+            self.backend.set_option(key, val)
         why = self.backend.prepare(gg.DTYPES[cfg["dtype"]], self.group_m, n, k, self.x.data_ptr(),
                                    self.w.data_ptr(), self.out.data_ptr(), stream.cuda_stream)
         if why:
@@ -566,7 +568,7 @@ def config_e_leg(torch, gg, dist, world, rank, local_rank, stream, steps, warmup
     return res
 
 
-def e2e_leg(torch, gg, prob, stream, dist, steps, variant):
+def e2e_leg(torch, gg, prob, stream, dist, steps):
     """End to end through the C ABI with host buffers: every step copies its x and w from pinned
     host memory and its output back. Two device buffer sets (each with its own prepared handle)
     let step i+1's host->device copies run on a copy stream while step i computes and copies
@@ -582,8 +584,8 @@ def e2e_leg(torch, gg, prob, stream, dist, steps, variant):
     sets = [(x, w, out, prob.backend)]
     x2, w2, out2 = torch.empty_like(x), torch.empty_like(w), torch.empty_like(out)
     b2 = gg.make_b200_backend()
-    if variant >= 0:
-        b2.set_option("variant", variant)
+    for key, val in prob.opts:
+        b2.set_option(key, val)
     if b2.prepare(gg.DTYPES[cfg["dtype"]], prob.group_m, cfg["n"], cfg["k"], x2.data_ptr(), w2.data_ptr(),
                   out2.data_ptr(), s):
         raise SystemExit("prepare refused the second buffer set")
@@ -642,6 +644,8 @@ def main():
     ap.add_argument("--allgather", action="store_true",
                     help="also time an NCCL all-gather of config E's sharded outputs")
     ap.add_argument("--variant", type=int, default=-1)
+    ap.add_argument("--opt", action="append", default=[], metavar="KEY=VALUE",
+                    help="gg_set_option knob for the headline problem's handle (repeatable), e.g. sched=0")
     ap.add_argument("--op", default="forward", choices=["forward", "dgrad", "wgrad"],
                     help="dgrad/wgrad: time a backward grouped GEMM on one GPU (not the headline line)")
     args = ap.parse_args()
@@ -673,7 +677,11 @@ def main():
     peaks, peak_src = measured_peaks()
     total_groups, (g0, g1) = shard_of(cfg, world, rank, gg)
     stream = torch.cuda.Stream()
-    prob = Problem(gg, torch, cfg, g0, g1, 1000 + rank, stream, args.variant)
+    opts = []
+    for kv in args.opt:
+        key, _, val = kv.partition("=")
+        opts.append((key, int(val)))
+    prob = Problem(gg, torch, cfg, g0, g1, 1000 + rank, stream, args.variant, opts)
     n, k = cfg["n"], cfg["k"]
 
     # ---- device-timed steps (inputs resident in HBM) ----
@@ -685,7 +693,7 @@ def main():
     roof = roofline(prob.flops, prob.alg_bytes, ms_step_rank, peaks, peak_src, load_traffic(args.config), detail)
 
     # ---- end to end through the C ABI with host buffers ----
-    e2e_ms, h2d, d2h = e2e_leg(torch, gg, prob, stream, dist, max(1, min(args.e2e_steps, args.steps)), args.variant)
+    e2e_ms, h2d, d2h = e2e_leg(torch, gg, prob, stream, dist, max(1, min(args.e2e_steps, args.steps)))
     e2e = {"value": round(total_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
            "steps": max(1, min(args.e2e_steps, args.steps)),

@@ -110,6 +110,7 @@ struct gg_handle {
     int opt_test_stall = 0;
     int opt_pdl = 1;
     int opt_store = -1;  // -1 auto, 0 = staging + TMA stores, 1 = direct stores
+    int opt_sched = 0;  // -1 auto (dynamic for multi-wave launches of whole tiles), 0 static, 1 dynamic
 
     // prepared state
     bool ready = false;
@@ -222,6 +223,10 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < -1 || value > 1)
             return fail(h, GG_ERR_ARG, "store must be -1 (auto), 0 (TMA stores) or 1 (direct stores)");
         h->opt_store = int(value);
+    } else if (!std::strcmp(key, "sched")) {
+        if (value < -1 || value > 1)
+            return fail(h, GG_ERR_ARG, "sched must be -1 (auto), 0 (static) or 1 (dynamic tile dispatch)");
+        h->opt_sched = int(value);
     } else if (!std::strcmp(key, "pdl")) {
         if (value != 0 && value != 1)
             return fail(h, GG_ERR_ARG, "pdl must be 0 or 1");
@@ -483,6 +488,7 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
         GG_CUDA(h, cudaMalloc(&h->d_meta, meta.size() * sizeof(int32_t)));
         h->meta_cap = meta.size();
     }
+    // status word [0] and the dynamic-dispatch tile counter [1], both zero between launches
     if (!h->d_status)
         GG_CUDA(h, cudaMalloc(&h->d_status, 16));
     GG_CUDA(h, cudaMemsetAsync(h->d_status, 0, 16, stream));
@@ -607,6 +613,11 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     kp.store_min_atoms = h->opt_store == 0 ? (1 << 30) : h->opt_store == 1 ? 0 : 16;
     kp.test_stall = h->opt_test_stall;
     kp.timeout_ns = uint64_t(h->opt_timeout_ms) * 1000000ull;
+    // Dynamic tile dispatch (whole tiles only): clusters take the next tile from a counter as they
+    // finish one, so tiles that share a weight panel run at the same time all through the launch
+    // (a static round-robin lets clusters drift apart); automatic for launches of more than one wave.
+    const bool dynamic = !partials && (h->opt_sched == 1 || (h->opt_sched < 0 && units * v.cg > h->grid));
+    kp.tile_ctr = dynamic ? reinterpret_cast<int32_t *>(h->d_status) + 1 : nullptr;
 
     GG_CUDA(h, cudaStreamSynchronize(stream));
 
@@ -622,8 +633,8 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     if (sk_tiles > 0)
         std::snprintf(form, sizeof(form), "split=1 stream_k=%lld tiles(<=%d pieces)", (long long)sk_tiles, ch.splits);
     else
-        std::snprintf(form, sizeof(form), "split=%d%s", ch.splits,
-                      split_tiles > 0 && split_tiles < tiles ? "(last wave)" : "");
+        std::snprintf(form, sizeof(form), "split=%d%s%s", ch.splits,
+                      split_tiles > 0 && split_tiles < tiles ? "(last wave)" : "", dynamic ? " dynamic" : "");
     char d[256];
     std::snprintf(d, sizeof(d), "gg_sm100<%s%s%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld %s grid=%d band=%d%s",
                   q.dtype == GG_BF16 ? "bf16" : "fp16", op == gg::kOpForward ? "" : ",", op == gg::kOpForward ? "" : op_name(op),
@@ -711,6 +722,8 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status) {
     GG_CUDA(h, cudaMemcpy(status, h->d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost));
     GG_CUDA(h, cudaMemset(h->d_status, 0, sizeof(uint32_t)));
     if (*status != 0) {
+        // an aborted launch can leave the dynamic-dispatch tile counter behind: clear it
+        GG_CUDA(h, cudaMemset(h->d_status, 0, 16));
         // an aborted launch can leave split-K arrival counts behind: clear them
         if (h->d_counters)
             GG_CUDA(h, cudaMemset(h->d_counters, 0, h->counters_cap));

@@ -116,6 +116,9 @@ struct KernelParams {
                               // registers; shorter tiles go through staging + TMA stores
     int32_t test_stall;   // test only: 1 = the first stage of cluster 0 is never loaded, so the
                           // MMA wait on it runs out and the status word reports it
+    int32_t *tile_ctr;    // non-null: dynamic tile dispatch (whole tiles only: splits <= 1, no
+                          // stream-K). Cluster c takes tile c first, then tile C + atomicAdd(tile_ctr, 1)
+                          // until past the last tile; 0 between launches (the last fetch resets it)
     uint64_t timeout_ns;
 };
 
@@ -143,14 +146,18 @@ template <int kCG, int kBN, int kAtoms> struct TileCfg {
     static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
     static constexpr int kTmemCols = (2 * kBN) <= 32 ? 32 : (2 * kBN) <= 64 ? 64 : (2 * kBN) <= 128 ? 128
                                      : (2 * kBN) <= 256 ? 256 : 512;
-    // barriers: full[S], empty[S], tmem_full[2], tmem_empty[2]; then tmem ptr and abort flag
     // Epilogue staging for TMA stores: per epilogue warp two 32-row x 64-column boxes (4 KB each,
     // 128-byte swizzle), after the ring.
     static constexpr int kStageOutBytes = 32 * 64 * 2;
     static constexpr int kOutOffset = kStages * kStageBytes;
     static constexpr int kOutBytes = GG_TMA_STORE ? 4 * 2 * kStageOutBytes : 0;
+    // barriers: full[S], empty[S], tmem_full[2], tmem_empty[2], sched_full[R], sched_empty[R]; then
+    // 16 bytes (TMEM base, abort flag, spare) and the R tile slots of the dynamic schedule
+    static constexpr int kSched = 4;  // tile slots between the dispatching producer and the other roles
     static constexpr int kBarOffset = kOutOffset + kOutBytes;
-    static constexpr int kSmemBytes = kBarOffset + (2 * kStages + 4) * 8 + 16 + 1024;  // + align slack
+    static constexpr int kNumBars = 2 * kStages + 4 + 2 * kSched;
+    static constexpr int kSlotOffset = kBarOffset + kNumBars * 8;
+    static constexpr int kSmemBytes = kSlotOffset + 16 + kSched * 4 + 1024;  // + align slack
     static_assert(kSmemBytes <= 232448, "over the 227 KB shared-memory limit");
     static_assert(kStages >= 2, "ring too shallow");
     static_assert(kAAtomBytes % 1024 == 0 && kBAtomBytes % 1024 == 0, "swizzle atoms 1024-byte aligned");
@@ -289,6 +296,19 @@ __host__ __device__ __forceinline__ Unit unit_at(const KernelParams &p, const Un
     return {s > 1 ? u - p.split_tiles * (s - 1) : u, 0, A, 0, 1};
 }
 
+// Dynamic tile dispatch (KernelParams::tile_ctr): cluster c runs tile c first; after each tile it
+// fetches a counter value v (atomicAdd) and runs tile C + v next, until that is past the last tile.
+// Each cluster makes exactly one fetch past the end, so a launch makes total_tiles fetches and the
+// one that returns total_tiles - 1 is the last: it resets the counter to 0 for the next launch.
+// (Host-callable, so that a CPU test can play out any order of fetches.)
+__host__ __device__ __forceinline__ int dispatched_tile(int fetched, int clusters, int total_tiles) {
+    const int t = clusters + fetched;
+    return t < total_tiles ? t : -1;
+}
+__host__ __device__ __forceinline__ bool is_last_fetch(int fetched, int total_tiles) {
+    return fetched == total_tiles - 1;
+}
+
 struct Abort {
     uint32_t *status;         // global
     volatile uint32_t *flag;  // this CTA's shared abort flag
@@ -349,8 +369,9 @@ __device__ __noinline__ bool wait_count(const int32_t *ctr, int want, const Abor
 
 // Bounded wait by a whole converged warp (the producer and MMA roles): every lane tests the
 // barrier and the warp agrees on the outcome (a wait that ran out in any lane ends the role in all).
+template <bool kClusterScope = false>
 __device__ __forceinline__ bool wait_all(uint32_t bar, uint32_t parity, const Abort &ab, uint32_t code) {
-    const bool ok = wait_one(bar, parity, ab, code);
+    const bool ok = wait_one<kClusterScope>(bar, parity, ab, code);
     return __all_sync(0xffffffffu, ok ? 1 : 0) != 0;
 }
 
@@ -418,8 +439,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto empty_bar = [&](int s) { return bar_base + 8u * (C::kStages + s); };
     auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * C::kStages + a); };
     auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * C::kStages + 2 + a); };
-    uint32_t *tmem_ptr_slot = reinterpret_cast<uint32_t *>(smem + C::kBarOffset + (2 * C::kStages + 4) * 8);
+    // dynamic tile dispatch: slot r holds the tile of units r, r + R, ... of this cluster
+    auto sfull_bar = [&](int r) { return bar_base + 8u * (2 * C::kStages + 4 + r); };
+    auto sempty_bar = [&](int r) { return bar_base + 8u * (2 * C::kStages + 4 + C::kSched + r); };
+    uint32_t *tmem_ptr_slot = reinterpret_cast<uint32_t *>(smem + C::kSlotOffset);
     volatile uint32_t *abort_flag = tmem_ptr_slot + 1;
+    const uint32_t sched_slots = smem_base + C::kSlotOffset + 16;
+    const volatile int32_t *sched_slot = reinterpret_cast<const volatile int32_t *>(smem + C::kSlotOffset + 16);
+    const bool dyn = p.tile_ctr != nullptr;
 
     const int warp = threadIdx.x / 32;
     const uint32_t lane = threadIdx.x & 31u;
@@ -436,6 +463,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int a = 0; a < 2; ++a) {
             ptx::mbar_init(tfull_bar(a), 1);         // one tcgen05.commit per tile
             ptx::mbar_init(tempty_bar(a), 4 * kCG);  // one arrive per epilogue warp of the pair
+        }
+        for (int r = 0; r < C::kSched; ++r) {
+            ptx::mbar_init(sfull_bar(r), 1);  // the pair leader's producer publishes the tile
+            // read by: the leader's MMA warp, every epilogue warp of the pair, the peer's producer
+            ptx::mbar_init(sempty_bar(r), 1 + 4 * kCG + (kCG - 1));
         }
         *abort_flag = 0u;
         ptx::fence_mbar_init();
@@ -494,8 +526,59 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t ph = 0;
             bool ok = true;
             int fenced_g = -1;  // wgrad: group whose tensor maps the warp has acquired
-            for (int i = 0; i < units.n && ok; ++i) {
-                const Unit un = unit_at(p, units, cluster_id, num_clusters, i);
+            const int issue_lane = __ffs(__ballot_sync(0xffffffffu, issue)) - 1;
+            int fetched = 0;  // dynamic dispatch, issuing lane of the leader: the next unit's fetch
+            for (int i = 0; ok; ++i) {
+                Unit un;
+                if (dyn) {
+                    // The pair leader's producer dispatches: unit 0 is tile cluster_id, each later
+                    // unit the tile its fetch (issued one unit ahead) returned; past the last tile it
+                    // publishes -1 and every role stops. The fetch that returns the launch's last
+                    // counter value resets the counter for the next launch.
+                    const int r = i % C::kSched;
+                    const uint32_t par = uint32_t(i / C::kSched) & 1u;
+                    int t = 0;
+                    if (leader) {
+                        if (issue) {
+                            t = i == 0 ? (cluster_id < p.total_tiles ? cluster_id : -1)
+                                       : dispatched_tile(fetched, num_clusters, p.total_tiles);
+                            if (i > 0 && is_last_fetch(fetched, p.total_tiles))
+                                atomicExch(p.tile_ctr, 0);
+                        }
+                        t = __shfl_sync(0xffffffffu, t, issue_lane);
+                        if (!wait_all(sempty_bar(r), par ^ 1u, ab, kStatusTimeout | kRoleProducer | 0x50u | uint32_t(r))) {
+                            ok = false;
+                            break;
+                        }
+                        if (issue) {
+                            ptx::st_shared_u32(sched_slots + 4u * r, uint32_t(t));
+                            ptx::mbar_arrive(sfull_bar(r));
+                            if constexpr (kCG == 2) {
+                                ptx::st_cluster_u32(ptx::mapa(sched_slots + 4u * r, 1), uint32_t(t));
+                                ptx::mbar_arrive_cluster(ptx::mapa(sfull_bar(r), 1));
+                            }
+                            if (t >= 0)
+                                fetched = atomicAdd(p.tile_ctr, 1);
+                        }
+                        __syncwarp();
+                    } else {
+                        if (!wait_all<true>(sfull_bar(r), par, ab, kStatusTimeout | kRoleProducer | 0x60u | uint32_t(r))) {
+                            ok = false;
+                            break;
+                        }
+                        t = sched_slot[r];
+                        if (issue)
+                            ptx::mbar_arrive_cluster(ptx::mapa(sempty_bar(r), 0));
+                        __syncwarp();
+                    }
+                    if (t < 0)
+                        break;
+                    un = Unit{t, 0, p.num_kb, 0, 1};
+                } else {
+                    if (i >= units.n)
+                        break;
+                    un = unit_at(p, units, cluster_id, num_clusters, i);
+                }
                 const TileCoord tc = decode_tile<C::kClusterM, kOp>(p, un.t, cursor);
                 const int atom0 = kOp == kOpWgrad ? 0 : un.atom0;
                 const int atom1 = kOp == kOpWgrad ? tc.red_atoms : un.atom1;
@@ -581,8 +664,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t ph = 0;
             bool ok = true;
             int cursor = 0;
-            for (int i = 0; i < units.n && ok; ++i, ++tl) {
-                const Unit un = unit_at(p, units, cluster_id, num_clusters, i);
+            for (int i = 0; ok; ++i, ++tl) {
+                Unit un;
+                if (dyn) {
+                    const int r = i % C::kSched;
+                    if (!wait_all<kCG == 2>(sfull_bar(r), uint32_t(i / C::kSched) & 1u, ab,
+                                            kStatusTimeout | kRoleMma | 0x60u | uint32_t(r))) {
+                        ok = false;
+                        break;
+                    }
+                    const int t = sched_slot[r];
+                    if (issue)
+                        ptx::mbar_arrive(sempty_bar(r));
+                    __syncwarp();
+                    if (t < 0)
+                        break;
+                    un = Unit{t, 0, p.num_kb, 0, 1};
+                } else {
+                    if (i >= units.n)
+                        break;
+                    un = unit_at(p, units, cluster_id, num_clusters, i);
+                }
                 int atom0 = un.atom0, atom1 = un.atom1;
                 if constexpr (kOp == kOpWgrad) {
                     atom0 = 0;
@@ -657,8 +759,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         int out_buf = 0;
         int cursor = 0;
         uint32_t tl = 0;
-        for (int i = 0; i < units.n; ++i, ++tl) {
-            const Unit un = unit_at(p, units, cluster_id, num_clusters, i);
+        const uint32_t sempty_leader0 = kCG == 2 ? ptx::mapa(sempty_bar(0), 0) : sempty_bar(0);
+        for (int i = 0;; ++i, ++tl) {
+            Unit un;
+            if (dyn) {
+                const int r = i % C::kSched;
+                int t = -1;
+                if (lane == 0) {
+                    if (wait_one<kCG == 2>(sfull_bar(r), uint32_t(i / C::kSched) & 1u, ab,
+                                           kStatusTimeout | kRoleEpilogue | 0x60u | uint32_t(r))) {
+                        t = sched_slot[r];
+                        if constexpr (kCG == 2)
+                            ptx::mbar_arrive_cluster(sempty_leader0 + 8u * r);
+                        else
+                            ptx::mbar_arrive(sempty_bar(r));
+                    }
+                }
+                t = __shfl_sync(0xffffffffu, t, 0);
+                if (t < 0)
+                    break;
+                un = Unit{t, 0, p.num_kb, 0, 1};
+            } else {
+                if (i >= units.n)
+                    break;
+                un = unit_at(p, units, cluster_id, num_clusters, i);
+            }
             const int t = un.t;
             const int split = un.piece;
             const int nsplit = un.npieces;

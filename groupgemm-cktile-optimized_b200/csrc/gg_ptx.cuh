@@ -286,6 +286,15 @@ __device__ __forceinline__ void tmem_tie(uint32_t (&r)[32]) {
                  : "memory");
 }
 
+// 32-bit stores into shared memory: this CTA's (shared::cta address) or any CTA's of the cluster
+// (shared::cluster address from mapa).
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
 // ---- MMA ----
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA with the 128-byte
 // swizzle: rows of 128 bytes (64 16-bit elements), 8-row swizzle atoms of 1024 bytes.

@@ -126,8 +126,11 @@ const char *gg_last_error(const gg_handle *h);
 
 /* Synchronises `stream`, then reads and clears the kernel's device status word: 0 when every
  * launch since the last read finished normally, otherwise the first bounded-wait timeout code
- * (0x1000 | role << 8 | barrier). No counterpart in the reference, whose kernel cannot time
- * out (its only device-side guard is a trap, ck_kernel/fast_epilogue.hpp:38-41). */
+ * (0x1000 | role << 8 | barrier). The outputs of every launch since the last read are then
+ * unreliable (an aborted launch stops part-way and can leave the dynamic-dispatch tile counter
+ * and split-K arrival counts behind; this call resets them, so later launches are sound again).
+ * No counterpart in the reference, whose kernel cannot time out (its only device-side guard is
+ * a trap, ck_kernel/fast_epilogue.hpp:38-41). */
 int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
 
 /* Override the automatic choices of gg_prepare / gg_prepare_grad (takes effect at the next
@@ -146,6 +149,12 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
  *                refused with "split" > 1, for wgrad, and where the tiling has no partial wave)
  *   "store"      -1 auto (direct stores from registers for tiles with >= 16 K atoms, staging +
  *                TMA stores for shorter ones), 0 = always TMA stores, 1 = always direct stores
+ *   "sched"      -1 auto (dynamic for launches of whole tiles with more tiles than CTAs / pairs),
+ *                0 = static round-robin (cluster c runs tiles c, c + C, ...), 1 = dynamic dispatch:
+ *                a cluster takes its next tile from a counter in the handle's device memory as it
+ *                finishes one, so tiles that share a weight panel stay in step all launch long.
+ *                The counter is zero between launches, so launches of one handle must not overlap
+ *                on the GPU (order them on one stream, as for any handle)
  *   "pdl"        1 (default) = launch with programmatic stream serialisation, so the launch and
  *                on-chip set-up overlap the previous kernel in the stream; 0 = plain launch
  *   "max_ctas"   cap on the persistent grid (0 = one CTA per SM)

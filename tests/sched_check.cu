@@ -9,6 +9,7 @@
 //   * a tile cut into pieces has workspace: n <= splits (the stride) and the tile is a split tile;
 //   * stream-K: every piece but piece 0 is the first unit of its cluster, so the fixed summer
 //     (piece 0) only ever waits for units that wait on nothing themselves (no circular wait).
+// The dynamic tile dispatch is played out in random fetch orders (check_dynamic).
 // Then decode_tile, for random group sizes (empty groups included), widths, bands and both raster
 // orders: tile indices map onto every (group, m-tile, n-tile) exactly once.
 // Prints "ok <launches> <units> <tables>" and exits 0, or prints the first violation and exits 1.
@@ -160,6 +161,50 @@ bool check_decode(const std::vector<int64_t> &group_m, int tiles_n, int band, in
     return true;
 }
 
+// Dynamic tile dispatch (dispatched_tile / is_last_fetch, as the kernel's producer uses them): C
+// clusters fetch from one counter in a random interleaving, two launches in a row on the same
+// counter. Every tile runs exactly once, each cluster's tiles increase (decode_tile's cursor only
+// moves forward), a launch makes exactly `tiles` fetches and leaves the counter at 0.
+bool check_dynamic(Rng &rng, int tiles, int C) {
+    int ctr = 0;
+    for (int launch = 0; launch < 2; ++launch) {
+        std::vector<int> cur(static_cast<size_t>(C), -1), last(static_cast<size_t>(C), -1);
+        std::vector<char> hit(static_cast<size_t>(tiles), 0);
+        std::vector<int> live;
+        for (int c = 0; c < C; ++c) {
+            cur[size_t(c)] = c < tiles ? c : -1;
+            if (cur[size_t(c)] >= 0)
+                live.push_back(c);
+        }
+        int fetches = 0;
+        while (!live.empty()) {
+            const size_t k = size_t(rng.range(0, int(live.size()) - 1));
+            const int c = live[k];
+            const int t = cur[size_t(c)];
+            if (t <= last[size_t(c)] || hit.at(size_t(t))++) {
+                std::printf("FAIL dynamic dispatch: tiles %d clusters %d tile %d repeated or out of order\n", tiles, C,
+                            t);
+                return false;
+            }
+            last[size_t(c)] = t;
+            const int v = ctr++;  // atomicAdd
+            ++fetches;
+            if (gg::is_last_fetch(v, tiles))
+                ctr = 0;
+            cur[size_t(c)] = gg::dispatched_tile(v, C, tiles);
+            if (cur[size_t(c)] < 0)
+                live.erase(live.begin() + long(k));
+        }
+        const bool all = std::all_of(hit.begin(), hit.end(), [](char h) { return h == 1; });
+        if (!all || ctr != 0 || fetches != tiles) {
+            std::printf("FAIL dynamic dispatch: tiles %d clusters %d covered %d counter %d fetches %d\n", tiles, C,
+                        int(all), ctr, fetches);
+            return false;
+        }
+    }
+    return true;
+}
+
 }  // namespace
 
 // `choose B,M,N,K ...`: the library's automatic choice for balanced problems on a B200 (148 SMs,
@@ -216,6 +261,12 @@ int main(int argc, char **argv) {
         if (!ok)
             return 1;
         ++decoded;
+    }
+    for (int n = 0; n < launches / 10; ++n) {
+        const int C = rng.range(1, 3) == 1 ? rng.range(1, 12) : rng.range(60, 148);
+        const int tiles = rng.range(1, 3) == 1 ? rng.range(C, 3 * C) : rng.range(C, 3000);
+        if (!check_dynamic(rng, tiles, C))
+            return 1;
     }
     std::printf("ok %d %lld %d\n", done, units, decoded);
     return 0;

@@ -3,8 +3,8 @@ against the CPU oracle (the reference's pass rule, bench/bench_main.cpp:264-270)
 
 Each case draws ragged group sizes (some empty), N and K with tails, a dtype, and a random mix
 of the options that change the kernel's schedule: variant, tile width, split count and form
-(every tile or only the last partial wave) or stream-K kind, raster order and band, and a capped
-grid (so small problems still have several waves). A combination the library refuses must be
+(every tile or only the last partial wave) or stream-K kind, raster order and band, a capped
+grid (so small problems still have several waves), and static or dynamic tile dispatch. A combination the library refuses must be
 refused with one of its documented reasons; every accepted one must match the oracle within
 tolerance, give the same bits on a second run, and leave the guard region after the output
 untouched.
@@ -48,6 +48,8 @@ def draw_case(rng):
         opts["band"] = int(rng.integers(1, 9))
     if rng.random() < 0.5:
         opts["max_ctas"] = int(rng.choice([4, 6, 10, 22]))
+    if rng.random() < 0.5:
+        opts["sched"] = int(rng.integers(0, 2))  # static or dynamic tile dispatch (else automatic)
     return group_m, n, k, op, dtype, opts
 
 

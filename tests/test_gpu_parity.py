@@ -512,3 +512,87 @@ def test_tile_widths_16_mod_32_with_partials_and_store_paths(gg, orc, opts):
     for r in res:
         bad, mx, first = orc.check16(r, ref, 0)
         assert bad == 0, (detail, bad, mx, first)
+
+
+@pytest.mark.parametrize("variant,bn,max_ctas", [(0, 256, 0), (0, 128, 12), (1, 192, 0), (1, 256, 7), (2, 128, 5)])
+@pytest.mark.parametrize("op", ["forward", "dgrad", "wgrad"])
+def test_dynamic_tile_dispatch_matches_static(gg, orc, variant, bn, max_ctas, op):
+    """Dynamic tile dispatch (clusters fetch their next tile from a counter) over many waves:
+    three launches in a row (the counter must be back at zero after each) give the same bits as
+    the static round-robin schedule, since every tile runs the same MMA sequence either way, and
+    pass the oracle's full compare."""
+    torch = _torch()
+    group_m, n, k = [900, 0, 333, 1500, 64], 1024, 520
+    s = torch.cuda.current_stream().cuda_stream
+    up = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda()  # noqa: E731
+    if op == "forward":
+        x, w = orc.make_inputs(group_m, n, k, 0)
+        ref, rows, cols = orc.grouped_gemm_f32(x, w, group_m, 0), sum(group_m), n
+        xd, wd = up(x), up(w)
+    else:
+        dy, x, w = orc.make_grad_inputs(group_m, n, k, 0)
+        dyd, xd, wd = up(dy), up(x), up(w)
+        if op == "dgrad":
+            ref, rows, cols = orc.grouped_dgrad_f32(dy, w, group_m, 0), sum(group_m), k
+        else:
+            ref, rows, cols = orc.grouped_wgrad_f32(dy, x, group_m, 0).reshape(-1, k), len(group_m) * n, k
+    results = {}
+    for sched in (0, 1):
+        out = torch.full((rows * cols + GUARD,), CANARY, dtype=torch.int16, device="cuda")
+        b = gg.B200Backend()
+        for key, val in {"variant": variant, "bn": bn, "max_ctas": max_ctas, "sched": sched}.items():
+            if val or key == "sched":
+                b.set_option(key, val)
+        if op == "forward":
+            why = b.prepare(0, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s)
+        elif op == "dgrad":
+            why = b.prepare_grad(gg.OP_DGRAD, 0, group_m, n, k, dy_ptr=dyd.data_ptr(), w_ptr=wd.data_ptr(),
+                                 dx_ptr=out.data_ptr(), stream=s)
+        else:
+            why = b.prepare_grad(gg.OP_WGRAD, 0, group_m, n, k, dy_ptr=dyd.data_ptr(), x_ptr=xd.data_ptr(),
+                                 dw_ptr=out.data_ptr(), stream=s)
+        assert why == "", why
+        assert ("dynamic" in b.detail()) == (sched == 1), b.detail()
+        runs = []
+        for _ in range(3):
+            out[:rows * cols].fill_(0)
+            b.run(s)
+            assert b.device_status(s) == 0, b.detail()
+            res = out.cpu().numpy().view(np.uint16)
+            assert np.all(res[rows * cols:] == CANARY), (b.detail(), "store past the end of out")
+            runs.append(res[:rows * cols].reshape(rows, cols).copy())
+        assert all(np.array_equal(runs[0], r) for r in runs[1:]), b.detail()
+        bad, mx, first = orc.check16(runs[0], ref, 0)
+        assert bad == 0, (b.detail(), bad, mx, first)
+        results[sched] = runs[0]
+        b.release()
+    assert np.array_equal(results[0], results[1])
+
+
+def test_dynamic_tile_dispatch_in_a_cuda_graph(gg, orc):
+    """A captured graph of several dynamic-dispatch launches replays correctly twice: each
+    launch leaves the tile counter at zero for the next."""
+    torch = _torch()
+    group_m, n, k = [700, 513, 64, 1000], 776, 192
+    x, w = orc.make_inputs(group_m, n, k, 0)
+    ref = orc.grouped_gemm_f32(x, w, group_m, 0)
+    xd, wd = upload(torch, x), upload(torch, w)
+    out = torch.zeros(sum(group_m) * n, dtype=torch.int16, device="cuda")
+    s = torch.cuda.Stream()
+    b = gg.B200Backend()
+    b.set_option("max_ctas", 8)
+    b.set_option("sched", 1)
+    assert b.prepare(0, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s.cuda_stream) == ""
+    assert "dynamic" in b.detail()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(3):
+            b.run(torch.cuda.current_stream().cuda_stream)
+    for _ in range(2):
+        out.zero_()
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        assert b.device_status(s.cuda_stream) == 0
+        got = out.cpu().numpy().view(np.uint16).reshape(-1, n)
+        assert orc.check16(got, ref, 0)[0] == 0
