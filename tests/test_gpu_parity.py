@@ -540,7 +540,8 @@ def test_dynamic_tile_dispatch_matches_static(gg, orc, variant, bn, max_ctas, op
     for sched in (0, 1):
         out = torch.full((rows * cols + GUARD,), CANARY, dtype=torch.int16, device="cuda")
         b = gg.B200Backend()
-        for key, val in {"variant": variant, "bn": bn, "max_ctas": max_ctas, "sched": sched}.items():
+        # split=1: no split-K (dynamic dispatch applies to launches of whole tiles)
+        for key, val in {"variant": variant, "bn": bn, "max_ctas": max_ctas, "sched": sched, "split": 1}.items():
             if val or key == "sched":
                 b.set_option(key, val)
         if op == "forward":
