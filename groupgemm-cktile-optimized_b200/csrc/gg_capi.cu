@@ -59,6 +59,7 @@ struct Variant {
     int smem;
     const void *fn[3][2];  // [operation: forward, dgrad, wgrad][dtype: bf16, fp16]
     int atoms;     // 64-element K atoms per stage
+    int (*stages_for)(int b_rows);  // ring stages of a launch whose tile loads b_rows B rows per CTA
 };
 
 template <int kCG, int kBN, int kAtoms, int kOp> void set_fns(Variant &v) {
@@ -68,7 +69,7 @@ template <int kCG, int kBN, int kAtoms, int kOp> void set_fns(Variant &v) {
 
 template <int kCG, int kBN, int kAtoms> Variant make_variant() {
     using C = gg::TileCfg<kCG, kBN, kAtoms>;
-    Variant v{kCG, kBN, C::kClusterM, C::kStages, C::kSmemBytes, {}, kAtoms};
+    Variant v{kCG, kBN, C::kClusterM, C::kStages, C::kSmemBytes, {}, kAtoms, &C::stages_for};
     set_fns<kCG, kBN, kAtoms, gg::kOpForward>(v);
     set_fns<kCG, kBN, kAtoms, gg::kOpDgrad>(v);
     set_fns<kCG, kBN, kAtoms, gg::kOpWgrad>(v);
@@ -638,7 +639,7 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     char d[256];
     std::snprintf(d, sizeof(d), "gg_sm100<%s%s%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld %s grid=%d band=%d%s",
                   q.dtype == GG_BF16 ? "bf16" : "fp16", op == gg::kOpForward ? "" : ",", op == gg::kOpForward ? "" : op_name(op),
-                  v.cluster_m, bn, gg::kBK * v.atoms, v.cg, v.stages, (long long)tiles, form, h->grid, band,
+                  v.cluster_m, bn, gg::kBK * v.atoms, v.cg, v.stages_for(bn / v.cg), (long long)tiles, form, h->grid, band,
                   raster ? "n" : "");
     h->detail = d;
     h->ready = true;

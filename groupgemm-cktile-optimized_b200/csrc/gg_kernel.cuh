@@ -143,19 +143,28 @@ template <int kCG, int kBN, int kAtoms> struct TileCfg {
     static constexpr int kABytes = kAtoms * kAAtomBytes;
     static constexpr int kBBytes = kAtoms * kBAtomBytes;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
+    static constexpr int kMaxStages = 8;
+    static constexpr int kStages = (kSmemBudget / kStageBytes) > kMaxStages ? kMaxStages : (kSmemBudget / kStageBytes);
+    static constexpr int kRingBytes = kStages * kStageBytes;  // sized for the widest tile (kBN)
+    // A launch with a narrower tile (bn < kBN) packs its stages tighter: each stage holds the A
+    // atoms and bn/kCG B rows per atom, so more of them fit in the same ring. Stage starts stay
+    // 1024-byte aligned (b_rows is a multiple of 8).
+    __host__ __device__ static constexpr int stage_bytes(int b_rows) { return kAtoms * (kAAtomBytes + b_rows * kBK * 2); }
+    __host__ __device__ static constexpr int stages_for(int b_rows) {
+        return kRingBytes / stage_bytes(b_rows) > kMaxStages ? kMaxStages : kRingBytes / stage_bytes(b_rows);
+    }
     static constexpr int kTmemCols = (2 * kBN) <= 32 ? 32 : (2 * kBN) <= 64 ? 64 : (2 * kBN) <= 128 ? 128
                                      : (2 * kBN) <= 256 ? 256 : 512;
     // Epilogue staging for TMA stores: per epilogue warp two 32-row x 64-column boxes (4 KB each,
     // 128-byte swizzle), after the ring.
     static constexpr int kStageOutBytes = 32 * 64 * 2;
-    static constexpr int kOutOffset = kStages * kStageBytes;
+    static constexpr int kOutOffset = kRingBytes;
     static constexpr int kOutBytes = GG_TMA_STORE ? 4 * 2 * kStageOutBytes : 0;
     // barriers: full[S], empty[S], tmem_full[2], tmem_empty[2], sched_full[R], sched_empty[R]; then
     // 16 bytes (TMEM base, abort flag, spare) and the R tile slots of the dynamic schedule
     static constexpr int kSched = 4;  // tile slots between the dispatching producer and the other roles
     static constexpr int kBarOffset = kOutOffset + kOutBytes;
-    static constexpr int kNumBars = 2 * kStages + 4 + 2 * kSched;
+    static constexpr int kNumBars = 2 * kMaxStages + 4 + 2 * kSched;
     static constexpr int kSlotOffset = kBarOffset + kNumBars * 8;
     static constexpr int kSmemBytes = kSlotOffset + 16 + kSched * 4 + 1024;  // + align slack
     static_assert(kSmemBytes <= 232448, "over the 227 KB shared-memory limit");
@@ -435,13 +444,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t smem_base = ptx::smem_addr(smem);
     const uint32_t bar_base = smem_base + C::kBarOffset;
+    // Ring geometry of this launch's tile width: stage count and bytes per stage and per B atom.
+    const int num_stages = C::stages_for(b_rows);
+    const uint32_t stage_bytes = uint32_t(C::stage_bytes(b_rows));
+    const uint32_t b_atom_bytes = uint32_t(b_rows * kBK * 2);
     auto full_bar = [&](int s) { return bar_base + 8u * s; };
-    auto empty_bar = [&](int s) { return bar_base + 8u * (C::kStages + s); };
-    auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * C::kStages + a); };
-    auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * C::kStages + 2 + a); };
+    auto empty_bar = [&](int s) { return bar_base + 8u * (C::kMaxStages + s); };
+    auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * C::kMaxStages + a); };
+    auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * C::kMaxStages + 2 + a); };
     // dynamic tile dispatch: slot r holds the tile of units r, r + R, ... of this cluster
-    auto sfull_bar = [&](int r) { return bar_base + 8u * (2 * C::kStages + 4 + r); };
-    auto sempty_bar = [&](int r) { return bar_base + 8u * (2 * C::kStages + 4 + C::kSched + r); };
+    auto sfull_bar = [&](int r) { return bar_base + 8u * (2 * C::kMaxStages + 4 + r); };
+    auto sempty_bar = [&](int r) { return bar_base + 8u * (2 * C::kMaxStages + 4 + C::kSched + r); };
     uint32_t *tmem_ptr_slot = reinterpret_cast<uint32_t *>(smem + C::kSlotOffset);
     volatile uint32_t *abort_flag = tmem_ptr_slot + 1;
     const uint32_t sched_slots = smem_base + C::kSlotOffset + 16;
@@ -456,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int num_clusters = gridDim.x / kCG;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::kStages; ++s) {
+        for (int s = 0; s < num_stages; ++s) {
             ptx::mbar_init(full_bar(s), 1);   // leader producer's arrive.expect_tx
             ptx::mbar_init(empty_bar(s), 1);  // one tcgen05.commit per use
         }
@@ -605,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     // K atoms of this stage that lie inside the unit's range (the rest would be zero fill)
                     const int na = min(kAtoms, atom1 - (atom0 + ks * kAtoms));
-                    const uint32_t a_dst = smem_base + uint32_t(s) * C::kStageBytes;
+                    const uint32_t a_dst = smem_base + uint32_t(s) * stage_bytes;
                     const uint32_t b_dst = a_dst + C::kABytes;
                     const uint32_t fb = full_leader0 + 8u * s;
                     // test hook: the leader skips its arrive and loads of cluster 0's first stage
@@ -617,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (a < na && !skip) {
                             const int k0 = (atom0 + ks * kAtoms + a) * kBK;
                             const uint32_t ad = a_dst + a * C::kAAtomBytes;
-                            const uint32_t bd = b_dst + a * C::kBAtomBytes;
+                            const uint32_t bd = b_dst + a * b_atom_bytes;
                             if constexpr (kAMn) {
                                 // wgrad A = dy^T: two 64-column boxes of the group's dy rows
                                 load_2d<kCG>(ad, map_a, fb, a_row, k0, issue);
@@ -637,16 +650,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                             }
                         }
                     }
-                    if (++s == C::kStages) {
+                    if (++s == num_stages) {
                         s = 0;
                         ph ^= 1u;
                     }
                 }
             }
             // Tail: every stage released, so no tcgen05.commit is still in flight to this CTA.
-            for (int i = 0; ok && i < C::kStages; ++i) {
+            for (int i = 0; ok && i < num_stages; ++i) {
                 ok = wait_all(empty_bar(s), ph ^ 1u, ab, kStatusTimeout | kRoleProducer | 0x80u);
-                if (++s == C::kStages) {
+                if (++s == num_stages) {
                     s = 0;
                     ph ^= 1u;
                 }
@@ -708,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     ptx::tc_fence_after();
                     const int na = min(kAtoms, atom1 - (atom0 + ks * kAtoms));
-                    const uint32_t a_addr = smem_base + uint32_t(s) * C::kStageBytes;
+                    const uint32_t a_addr = smem_base + uint32_t(s) * stage_bytes;
                     const uint64_t adesc = kAMn ? ptx::sw128_mnmajor_desc(a_addr) : ptx::sw128_kmajor_desc(a_addr);
                     const uint64_t bdesc = kBMn ? ptx::sw128_mnmajor_desc(a_addr + C::kABytes)
                                                 : ptx::sw128_kmajor_desc(a_addr + C::kABytes);
@@ -722,7 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
                                 // atom a, then the kk-th 16-element K step inside the atom
                                 const uint64_t da = uint64_t((a * C::kAAtomBytes + kk * kStepA) >> 4);
-                                const uint64_t db = uint64_t((a * C::kBAtomBytes + kk * kStepB) >> 4);
+                                const uint64_t db = uint64_t((a * b_atom_bytes + kk * kStepB) >> 4);
                                 ptx::umma_f16<kCG>(d_tmem, adesc + da, bdesc + db, idesc,
                                                    (ks | a | kk) != 0 ? 1u : 0u, issue);
                             }
@@ -731,7 +744,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ptx::umma_commit<kCG>(empty_bar(s), issue);
                     if constexpr (kCG == 2)
                         ptx::umma_commit<kCG>(ptx::mapa(empty_bar(s), 1), issue);
-                    if (++s == C::kStages) {
+                    if (++s == num_stages) {
                         s = 0;
                         ph ^= 1u;
                     }
@@ -759,7 +772,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         int out_buf = 0;
         int cursor = 0;
         uint32_t tl = 0;
-        const uint32_t sempty_leader0 = kCG == 2 ? ptx::mapa(sempty_bar(0), 0) : sempty_bar(0);
         for (int i = 0;; ++i, ++tl) {
             Unit un;
             if (dyn) {
@@ -770,7 +782,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                            kStatusTimeout | kRoleEpilogue | 0x60u | uint32_t(r))) {
                         t = sched_slot[r];
                         if constexpr (kCG == 2)
-                            ptx::mbar_arrive_cluster(sempty_leader0 + 8u * r);
+                            ptx::mbar_arrive_cluster(ptx::mapa(sempty_bar(r), 0));
                         else
                             ptx::mbar_arrive(sempty_bar(r));
                     }
@@ -931,7 +943,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // chunk by chunk. The other pieces' blocks stream in (chunk, piece) order through a
                 // ring of kPrefetch register buffers, so that many L2 reads are in flight at once;
                 // the ring is indexed at compile time (block b sits in buffer b % kPrefetch).
-                constexpr int kPrefetch = 3;
+                constexpr int kPrefetch = 2;
                 const int others = nsplit - 1;
                 const int nb = nch * others;
                 auto load_blk = [&](int b, float4 (&dst)[8]) {
@@ -994,17 +1006,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             } else {
+                // Direct stores, two 32-column chunks per TMEM wait: both loads are in flight
+                // before the wait, then both chunks are converted and stored.
 #pragma unroll 1
-                for (int c = c_tma; store_out && c < nch; ++c) {
-                    uint32_t r[32];
-                    ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
-                    ptx::tmem_wait_ld(r);
-                    if (zero_tile) {
+                for (int c = c_tma; store_out && c < nch; c += 2) {
+                    uint32_t rr[2][32];
+                    const bool two = c + 1 < nch;
+                    ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), rr[0]);
+                    if (two)
+                        ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + 1) * 32), rr[1]);
+                    ptx::tmem_wait_ld(rr[0]);
+                    ptx::tmem_tie(rr[1]);
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            r[j] = 0u;
+                    for (int hh = 0; hh < 2; ++hh) {
+                        if (hh == 1 && !two)
+                            break;
+                        if (zero_tile) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                rr[hh][j] = 0u;
+                        }
+                        store_chunk(c + hh, rr[hh]);
                     }
-                    store_chunk(c, r);
                 }
             }
             ptx::tc_fence_before();
