@@ -343,6 +343,9 @@ def run_backward(args, cfg):
     be = gg.make_b200_backend()
     if args.variant >= 0:
         be.set_option("variant", args.variant)
+    for kv in args.opt:
+        key, _, val = kv.partition("=")
+        be.set_option(key, int(val))
     if op == gg.OP_DGRAD:
         why = be.prepare_grad(op, dtype, group_m, n, k, dy_ptr=dy.data_ptr(), w_ptr=b_op.data_ptr(),
                               dx_ptr=out.data_ptr(), stream=s)

@@ -111,6 +111,7 @@ struct gg_handle {
     int opt_test_stall = 0;
     int opt_pdl = 1;
     int opt_store = -1;  // -1 auto, 0 = staging + TMA stores, 1 = direct stores
+    int opt_half = -1;   // -1 auto (= on where a group ends in a remainder of at most 128 rows), 0 off, 1 on
     int opt_sched = 0;  // -1 auto (dynamic for multi-wave launches of whole tiles), 0 static, 1 dynamic
 
     // prepared state
@@ -130,6 +131,7 @@ struct gg_handle {
     size_t gmaps_cap = 0;            // maps
     int op = 0;                      // gg::kOpForward / kOpDgrad / kOpWgrad
     CUtensorMap tmap_a{}, tmap_b{}, tmap_out{};
+    CUtensorMap tmap_a_half{};  // A in 64-row boxes, for half-height pair tiles
     gg::KernelParams params{};
     int grid = 0;
     const void *fn = nullptr;
@@ -224,6 +226,10 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < -1 || value > 1)
             return fail(h, GG_ERR_ARG, "store must be -1 (auto), 0 (TMA stores) or 1 (direct stores)");
         h->opt_store = int(value);
+    } else if (!std::strcmp(key, "half_tiles")) {
+        if (value < -1 || value > 1)
+            return fail(h, GG_ERR_ARG, "half_tiles must be -1 (auto), 0 (off) or 1 (on)");
+        h->opt_half = int(value);
     } else if (!std::strcmp(key, "sched")) {
         if (value < -1 || value > 1)
             return fail(h, GG_ERR_ARG, "sched must be -1 (auto), 0 (static) or 1 (dynamic tile dispatch)");
@@ -520,17 +526,28 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     GG_CUDA(h, cudaMemcpyAsync(h->d_meta, meta.data(), meta.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
                                stream));
 
+    // Half-height pair tiles for groups that end in a remainder of at most 128 rows (pair variant,
+    // forward / dgrad, whole tiles, a tile width the M = 128 pair MMA takes).
+    bool half_tiles = false;
+    if (v.cg == 2 && op != gg::kOpWgrad && !partials && bn % 32 == 0 && h->opt_half != 0)
+        for (int g = 0; g < G && !half_tiles; ++g)
+            half_tiles = (q.group_m[g] % 256) != 0 && (q.group_m[g] % 256) <= 128;
+
     // ---- TMA descriptors ----
     const CUtensorMapDataType dt =
         q.dtype == GG_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const uint32_t b_box = uint32_t(bn / v.cg);
     h->tmap_a = CUtensorMap{};
+    h->tmap_a_half = CUtensorMap{};
     h->tmap_b = CUtensorMap{};
     h->tmap_out = CUtensorMap{};
     std::vector<CUtensorMap> gmaps;
     if (op == gg::kOpForward && total_m > 0) {
         if (encode_2d(encode, &h->tmap_a, dt, q.a, q.k, total_m, gg::kBK, gg::kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
             return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed");
+        if (half_tiles && encode_2d(encode, &h->tmap_a_half, dt, q.a, q.k, total_m, gg::kBK, 64,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(x, 64-row boxes) failed");
         if (encode_w(encode, &h->tmap_b, dt, q.b, q.n, q.k, G, gg::kBK, b_box))
             return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(w) failed");
         // out [sum(M), N]: the epilogue's TMA stores, 32 rows x 64 columns per box
@@ -540,6 +557,9 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
         // A = dy [sum(M), N], K-major over N; B = w[g] read as 64 (K) x 64 (N) MN-major boxes
         if (encode_2d(encode, &h->tmap_a, dt, q.a, q.n, total_m, gg::kBK, gg::kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
             return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(dy) failed");
+        if (half_tiles && encode_2d(encode, &h->tmap_a_half, dt, q.a, q.n, total_m, gg::kBK, 64,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+            return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(dy, 64-row boxes) failed");
         if (encode_w(encode, &h->tmap_b, dt, q.b, q.n, q.k, G, 64, gg::kBK))
             return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(w) failed");
         if (encode_2d(encode, &h->tmap_out, dt, q.out, q.k, total_m, 64, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE))
@@ -613,6 +633,7 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     // epilogue store path: direct stores for tiles with >= 16 K atoms (1024 of reduction)
     kp.store_min_atoms = h->opt_store == 0 ? (1 << 30) : h->opt_store == 1 ? 0 : 16;
     kp.test_stall = h->opt_test_stall;
+    kp.half_tiles = half_tiles && total_m > 0 ? 1 : 0;
     kp.timeout_ns = uint64_t(h->opt_timeout_ms) * 1000000ull;
     // Dynamic tile dispatch (whole tiles only): clusters take the next tile from a counter as they
     // finish one, so tiles that share a weight panel run at the same time all through the launch
@@ -634,8 +655,9 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     if (sk_tiles > 0)
         std::snprintf(form, sizeof(form), "split=1 stream_k=%lld tiles(<=%d pieces)", (long long)sk_tiles, ch.splits);
     else
-        std::snprintf(form, sizeof(form), "split=%d%s%s", ch.splits,
-                      split_tiles > 0 && split_tiles < tiles ? "(last wave)" : "", dynamic ? " dynamic" : "");
+        std::snprintf(form, sizeof(form), "split=%d%s%s%s", ch.splits,
+                      split_tiles > 0 && split_tiles < tiles ? "(last wave)" : "", dynamic ? " dynamic" : "",
+                      half_tiles ? " half-tiles" : "");
     char d[256];
     std::snprintf(d, sizeof(d), "gg_sm100<%s%s%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld %s grid=%d band=%d%s",
                   q.dtype == GG_BF16 ? "bf16" : "fp16", op == gg::kOpForward ? "" : ",", op == gg::kOpForward ? "" : op_name(op),
@@ -708,7 +730,7 @@ int gg_run(gg_handle *h, gg_stream_t stream) {
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = h->opt_pdl ? 2 : 1;
-    void *args[4] = {&h->tmap_a, &h->tmap_b, &h->tmap_out, &h->params};
+    void *args[5] = {&h->tmap_a, &h->tmap_b, &h->tmap_out, &h->tmap_a_half, &h->params};
     GG_CUDA(h, cudaLaunchKernelExC(&cfg, h->fn, args));
     return GG_OK;
 }
@@ -954,7 +976,7 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
 
     const CUtensorMapDataType dt =
         p->dtype == GG_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    CUtensorMap tmap_a, tmap_b, tmap_out;
+    CUtensorMap tmap_a, tmap_b, tmap_out, tmap_unused{};  // no half-height tiles on this path
     if (encode_2d(encode, &tmap_a, dt, p->x, p->k, total_m, gg::kBK, gg::kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)) {
         copy_msg(why, why_len, "cuTensorMapEncodeTiled(x) failed");
         return GG_ERR_CUDA;
@@ -1002,7 +1024,7 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    void *args[4] = {&tmap_a, &tmap_b, &tmap_out, &kp};
+    void *args[5] = {&tmap_a, &tmap_b, &tmap_out, &tmap_unused, &kp};
     if ((e = cudaLaunchKernelExC(&cfg, v.fn[gg::kOpForward][p->dtype], args)) != cudaSuccess)
         return cuda_fail("kernel launch", e);
 

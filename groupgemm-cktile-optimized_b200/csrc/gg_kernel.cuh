@@ -116,6 +116,8 @@ struct KernelParams {
                               // registers; shorter tiles go through staging + TMA stores
     int32_t test_stall;   // test only: 1 = the first stage of cluster 0 is never loaded, so the
                           // MMA wait on it runs out and the status word reports it
+    int32_t half_tiles;   // 1: a group's last m-tile with at most 128 rows runs half height (pair
+                          // variant, forward / dgrad, whole tiles; needs bn % 32 == 0)
     int32_t *tile_ctr;    // non-null: dynamic tile dispatch (whole tiles only: splits <= 1, no
                           // stream-K). Cluster c takes tile c first, then tile C + atomicAdd(tile_ctr, 1)
                           // until past the last tile; 0 between launches (the last fetch resets it)
@@ -177,7 +179,21 @@ struct TileCoord {
     int rows;          // output rows of the group (tokens for forward/dgrad, N for wgrad)
     int out_row0;      // first output row of the group
     int red_atoms;     // 64-wide reduction atoms of the group
+    bool half;         // a half-height pair tile (see is_half_tile)
 };
+
+// Half-height pair tiles (KernelParams::half_tiles): when the last m-tile of a group holds at most
+// 128 of the 256 rows a CTA pair covers, it runs as a 128-row tile (64 rows per CTA) with an
+// M = 128 cta_group::2 MMA, which the tensor cores execute at the same rate per row as M = 256, so
+// a small expert's remainder costs half a tile instead of a padded whole one. Forward and dgrad
+// (tiles over tokens); wgrad tiles run over the weight rows and never use them.
+template <int kClusterM, int kOp>
+__host__ __device__ __forceinline__ bool is_half_tile(int half_tiles, int rows, int mt) {
+    if (kClusterM != 256 || kOp == 2 || !half_tiles)
+        return false;
+    const int rem = rows & 255;
+    return rem != 0 && rem <= 128 && mt == (rows - 1) / 256;
+}
 
 // Map a linear tile index to (group, m-tile, n-tile). Within a group, tiles are rastered in
 // bands (the role CK's GemmSpatiallyLocalTilePartitioner<8,4> plays in the reference,
@@ -232,6 +248,7 @@ __host__ __device__ __forceinline__ TileCoord decode_tile(const KernelParams &p,
         tc.mt = r / cols;
         tc.nt = b * p.band + (r - tc.mt * cols);
     }
+    tc.half = is_half_tile<kClusterM, kOp>(p.half_tiles, tc.rows, tc.mt);
     return tc;
 }
 
@@ -427,6 +444,7 @@ template <typename T, int kCG, int kBN, int kAtoms, int kOp>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_sm100(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                        const __grid_constant__ CUtensorMap tmap_out,
+                       const __grid_constant__ CUtensorMap tmap_a_half,  // A in 64-row boxes (half tiles)
                        const __grid_constant__ KernelParams p) {
     using C = TileCfg<kCG, kBN, kAtoms>;
     // A is MN-major for wgrad (dy^T), B is MN-major for both backward operations.
@@ -438,6 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int bn = p.bn;
     const int b_rows = bn / kCG;
     const uint32_t idesc = ptx::f16_idesc(Fmt<T>::kUmma, kBM * kCG, bn, kAMn ? 1u : 0u, kBMn ? 1u : 0u);
+    const uint32_t idesc_half = ptx::f16_idesc(Fmt<T>::kUmma, 128, bn, 0u, kBMn ? 1u : 0u);  // M = 128 pair tile
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the 128-byte swizzle atoms.
@@ -493,6 +512,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (GG_TMA_STORE)
             ptx::prefetch_tmap(&tmap_out);
+        if (p.half_tiles)
+            ptx::prefetch_tmap(&tmap_a_half);
     }
     if (warp == 1) {
         ptx::tmem_alloc<kCG>(ptx::smem_addr(tmem_ptr_slot), C::kTmemCols);
@@ -506,15 +527,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_ptr_slot;
     // Everything above is on-chip set-up; with programmatic dependent launch it overlaps the
     // previous kernel's tail. The group-offset table is written by the host before the stream
-    // reaches this launch (prepare synchronises its stream), never by a preceding kernel, so the
-    // first tile's look-up may also run before the dependency wait, bringing the table's first
-    // lines into this SM's cache meanwhile. Every other global access comes after the wait.
+    // reaches this launch (prepare synchronises its stream), or by gg_run_noalloc's publish kernel,
+    // which precedes a launch made without programmatic serialisation; never by a kernel this
+    // launch may overlap. So the first tile's look-up may run before the dependency wait. Every
+    // other global access comes after the wait.
     const UnitList units = units_of(p, cluster_id, num_clusters);
-    if (threadIdx.x == 0 && units.n > 0) {
-        int cur = 0;
-        const TileCoord tc0 = decode_tile<C::kClusterM, kOp>(p, unit_at(p, units, cluster_id, num_clusters, 0).t, cur);
-        tmem_ptr_slot[2] = uint32_t(tc0.g + tc0.rows);  // keeps the loads (slot otherwise unused)
-    }
+    // The producer decodes its first unit's tile here, so that its first TMA loads can be issued
+    // right after the dependency wait (decoding after it would wait on dependent global loads).
+    // (Unit 0 is tile cluster_id with dynamic dispatch too: that needs whole tiles.)
+    TileCoord first_tc{};
+    int first_cursor = 0;
+    if (warp <= 1 && units.n > 0)  // the producer, and the MMA warp (tile height, wgrad reduction)
+        first_tc = decode_tile<C::kClusterM, kOp>(p, unit_at(p, units, cluster_id, num_clusters, 0).t, first_cursor);
     ptx::griddep_wait();
     // TMA loads and stores go through the async proxy; a proxy fence orders them after the
     // generic-proxy writes of the previous kernel that the wait made visible (a conservative
@@ -592,12 +616,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     un = unit_at(p, units, cluster_id, num_clusters, i);
                 }
-                const TileCoord tc = decode_tile<C::kClusterM, kOp>(p, un.t, cursor);
+                TileCoord tc;
+                if (i == 0) {  // decoded before the dependency wait
+                    tc = first_tc;
+                    cursor = first_cursor;
+                } else {
+                    tc = decode_tile<C::kClusterM, kOp>(p, un.t, cursor);
+                }
                 const int atom0 = kOp == kOpWgrad ? 0 : un.atom0;
                 const int atom1 = kOp == kOpWgrad ? tc.red_atoms : un.atom1;
                 const int num_ks = (atom1 - atom0 + kAtoms - 1) / kAtoms;
-                // A: first row (forward/dgrad: token row; wgrad: row of dw[g], a column of dy)
-                const int a_row = (kOp == kOpWgrad ? 0 : tc.out_row0) + tc.mt * C::kClusterM + int(cta_rank) * kBM;
+                // A: first row (forward/dgrad: token row; wgrad: row of dw[g], a column of dy); a
+                // half tile gives each CTA 64 rows, loaded through the 64-row map
+                const bool half = tc.half;
+                const int a_row = (kOp == kOpWgrad ? 0 : tc.out_row0) + tc.mt * C::kClusterM + int(cta_rank) * (half ? 64 : kBM);
+                const uint32_t a_atom_load = half ? uint32_t(C::kAAtomBytes / 2) : uint32_t(C::kAAtomBytes);
                 // B: first weight row (forward) / first output column (backward) of this CTA
                 const int b_row = tc.nt * bn + int(cta_rank) * b_rows;
                 const void *map_a = &tmap_a;
@@ -623,7 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t fb = full_leader0 + 8u * s;
                     // test hook: the leader skips its arrive and loads of cluster 0's first stage
                     const bool skip = p.test_stall != 0 && cluster_id == 0 && leader && ks == 0 && i == 0;
-                    ptx::mbar_arrive_expect_tx(full_bar(s), uint32_t(kCG * na * (C::kAAtomBytes + b_rows * kBK * 2)),
+                    ptx::mbar_arrive_expect_tx(full_bar(s), uint32_t(kCG * na) * (a_atom_load + b_atom_bytes),
                                                leader && !skip ? issue : 0u);
 #pragma unroll
                     for (int a = 0; a < kAtoms; ++a) {
@@ -636,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 load_2d<kCG>(ad, map_a, fb, a_row, k0, issue);
                                 load_2d<kCG>(ad + kMnBoxBytes, map_a, fb, a_row + 64, k0, issue);
                             } else {
-                                load_2d<kCG>(ad, map_a, fb, k0, a_row, issue);
+                                load_2d<kCG>(ad, half ? static_cast<const void *>(&tmap_a_half) : map_a, fb, k0, a_row, issue);
                             }
                             if constexpr (kOp == kOpForward) {
                                 load_3d<kCG>(bd, map_b, fb, k0, b_row, tc.g, issue);
@@ -699,10 +732,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                     un = unit_at(p, units, cluster_id, num_clusters, i);
                 }
                 int atom0 = un.atom0, atom1 = un.atom1;
-                if constexpr (kOp == kOpWgrad) {
-                    atom0 = 0;
-                    atom1 = decode_tile<C::kClusterM, kOp>(p, un.t, cursor).red_atoms;  // 0 for an empty group
+                bool half = false;
+                if (kOp == kOpWgrad || p.half_tiles) {
+                    TileCoord tcm;
+                    if (i == 0) {  // decoded before the dependency wait
+                        tcm = first_tc;
+                        cursor = first_cursor;
+                    } else {
+                        tcm = decode_tile<C::kClusterM, kOp>(p, un.t, cursor);
+                    }
+                    if constexpr (kOp == kOpWgrad) {
+                        atom0 = 0;
+                        atom1 = tcm.red_atoms;  // 0 for an empty group
+                    }
+                    half = tcm.half;
                 }
+                const uint32_t idesc_t = half ? idesc_half : idesc;
                 const int num_ks = (atom1 - atom0 + kAtoms - 1) / kAtoms;
                 const int acc = int(tl & 1u);
                 const uint32_t acc_ph = (tl >> 1) & 1u;
@@ -736,7 +781,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 // atom a, then the kk-th 16-element K step inside the atom
                                 const uint64_t da = uint64_t((a * C::kAAtomBytes + kk * kStepA) >> 4);
                                 const uint64_t db = uint64_t((a * b_atom_bytes + kk * kStepB) >> 4);
-                                ptx::umma_f16<kCG>(d_tmem, adesc + da, bdesc + db, idesc,
+                                ptx::umma_f16<kCG>(d_tmem, adesc + da, bdesc + db, idesc_t,
                                                    (ks | a | kk) != 0 ? 1u : 0u, issue);
                             }
                         }
@@ -809,7 +854,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int m = tc.rows;
             // wgrad of an expert without tokens: no MMA ran, the tile is written as zeros
             const bool zero_tile = kOp == kOpWgrad && tc.red_atoms == 0;
-            const int local_row = tc.mt * C::kClusterM + int(cta_rank) * kBM + row_in_cta;
+            // A half tile's accumulator (M = 128 pair MMA): CTA r holds its 64 rows in TMEM lanes
+            // 0-63 for output columns [0, bn/2) and again in lanes 64-127 for [bn/2, bn), in
+            // bn/2 TMEM columns. So warp quarter q stores rows (q & 1) * 32 + lane of the CTA's 64,
+            // columns from (q >> 1) * bn/2; a whole tile's quarter stores rows q * 32 + lane, all bn.
+            const bool half = tc.half;
+            const int local_row = half ? tc.mt * C::kClusterM + int(cta_rank) * 64 + (q & 1) * 32 + int(lane)
+                                       : tc.mt * C::kClusterM + int(cta_rank) * kBM + row_in_cta;
+            const int tile_w = half ? bn / 2 : bn;                      // output columns of this warp
+            const int col0 = tc.nt * bn + (half && q >= 2 ? bn / 2 : 0);  // its first output column
             const bool row_ok = local_row < m;
             const int64_t grow = int64_t(g_row0) + local_row;
             T *orow = out + grow * p.n;
@@ -817,7 +870,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool store_out = true;
             // 32-column chunks of the tile (a tile width of 16 mod 32 ends in a half chunk: it is read
             // whole from TMEM, inside the accumulator buffer, and its upper 16 columns are dropped)
-            const int nch = (bn + 31) / 32;
+            const int nch = (tile_w + 31) / 32;
             // split-K: first float4 of this warp's workspace region (p.splits x nch blocks of 4 KB)
             const int64_t ws_warp = ((int64_t(t) * kCG + int(cta_rank)) * 4 + q) * int64_t(p.splits) * nch * 256;
             if (nsplit > 1) {
@@ -871,7 +924,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // epilogue is hidden behind the next main loop, and skipping the staging spares the
             // shared-memory bandwidth the main loop uses (measured: +2-5% on configs D, E, P).
             const int slab_rows_ok = m - (tc.mt * C::kClusterM + int(cta_rank) * kBM + q * 32);
-            const int c_tma = (GG_TMA_STORE && nsplit == 1 && slab_rows_ok >= 32 && tc.red_atoms < p.store_min_atoms)
+            const int c_tma = (GG_TMA_STORE && !half && nsplit == 1 && slab_rows_ok >= 32 && tc.red_atoms < p.store_min_atoms)
                                   ? (bn / 64) * 2 : 0;
 #pragma unroll 1
             for (int c = 0; c < c_tma; c += 2) {
@@ -910,14 +963,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 out_buf ^= 1;
             }
-            const int col_end = min(p.n, tc.nt * bn + bn);  // tile's last column + 1
+            const int col_end = min(p.n, col0 + tile_w);  // this warp's last column + 1
             // Store 32 accumulator columns (fp32 bits) of this lane's row: whole 32-byte sectors
             // where the row allows (N % 16 == 0 keeps rows 32-byte aligned), else 16-byte pieces;
             // columns past the tile or past N are skipped in 8s.
             auto store_chunk = [&](int c, const uint32_t (&r)[32]) {
                 if (!row_ok)
                     return;
-                const int col = tc.nt * bn + c * 32;
+                const int col = col0 + c * 32;
                 uint32_t h[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j)

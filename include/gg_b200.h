@@ -155,6 +155,11 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
  *                finishes one, so tiles that share a weight panel stay in step all launch long.
  *                The counter is zero between launches, so launches of one handle must not overlap
  *                on the GPU (order them on one stream, as for any handle)
+ *   "half_tiles" -1 auto (= on), 0 off, 1 on: with the 2-CTA variant (forward and dgrad, no
+ *                split-K or stream-K, a tile width that is a multiple of 32), a group whose last
+ *                256-row tile holds at most 128 rows runs that tile half height (an M = 128 pair
+ *                MMA, 64 rows per CTA, same tensor rate per row), so a small expert's remainder
+ *                costs half a tile, not a padded whole one (skewed routing)
  *   "pdl"        1 (default) = launch with programmatic stream serialisation, so the launch and
  *                on-chip set-up overlap the previous kernel in the stream; 0 = plain launch
  *   "max_ctas"   cap on the persistent grid (0 = one CTA per SM)

@@ -9,7 +9,8 @@
 //   * a tile cut into pieces has workspace: n <= splits (the stride) and the tile is a split tile;
 //   * stream-K: every piece but piece 0 is the first unit of its cluster, so the fixed summer
 //     (piece 0) only ever waits for units that wait on nothing themselves (no circular wait).
-// The dynamic tile dispatch is played out in random fetch orders (check_dynamic).
+// The dynamic tile dispatch is played out in random fetch orders (check_dynamic), and the
+// half-height tile flag is checked on every decoded tile.
 // Then decode_tile, for random group sizes (empty groups included), widths, bands and both raster
 // orders: tile indices map onto every (group, m-tile, n-tile) exactly once.
 // Prints "ok <launches> <units> <tables>" and exits 0, or prints the first violation and exits 1.
@@ -150,6 +151,15 @@ bool check_decode(const std::vector<int64_t> &group_m, int tiles_n, int band, in
         if (!ok) {
             std::printf("FAIL decode_tile: cm %d op %d G %d tiles_n %d band %d raster %d tile %lld\n", kCM, kOp, G,
                         tiles_n, band, raster, (long long)t);
+            return false;
+        }
+        // half-height pair tiles: exactly the last m-tile of a group whose remainder is 1..128 rows
+        // (tiles of 256 rows, forward / dgrad); never with the option off, for 128-row tiles or wgrad
+        const int64_t rem = m_rows % 256;
+        const bool want_half = kCM == 256 && kOp != gg::kOpWgrad && rem != 0 && rem <= 128 && tc.mt == tiles_m - 1;
+        const bool got_half = gg::is_half_tile<kCM, kOp>(1, tc.rows, tc.mt);
+        if (got_half != want_half || tc.half || gg::is_half_tile<kCM, kOp>(0, tc.rows, tc.mt)) {
+            std::printf("FAIL half-tile flag: cm %d op %d rows %lld mt %d\n", kCM, kOp, (long long)m_rows, tc.mt);
             return false;
         }
         const int64_t idx = tile_off[size_t(g)] + int64_t(tc.mt) * tiles_n + tc.nt;

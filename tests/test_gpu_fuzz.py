@@ -50,6 +50,8 @@ def draw_case(rng):
         opts["max_ctas"] = int(rng.choice([4, 6, 10, 22]))
     if rng.random() < 0.5:
         opts["sched"] = int(rng.integers(0, 2))  # static or dynamic tile dispatch (else automatic)
+    if rng.random() < 0.3:
+        opts["half_tiles"] = 0  # otherwise automatic: half-height last tiles where a group allows
     return group_m, n, k, op, dtype, opts
 
 

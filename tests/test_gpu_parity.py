@@ -597,3 +597,77 @@ def test_dynamic_tile_dispatch_in_a_cuda_graph(gg, orc):
         assert b.device_status(s.cuda_stream) == 0
         got = out.cpu().numpy().view(np.uint16).reshape(-1, n)
         assert orc.check16(got, ref, 0)[0] == 0
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+@pytest.mark.parametrize("bn", [256, 192, 160, 128])
+@pytest.mark.parametrize("op", ["forward", "dgrad"])
+def test_half_height_pair_tiles(gg, orc, dtype, bn, op):
+    """Groups whose last m-tile holds at most 128 rows run it as a 128-row pair tile (M = 128
+    cta_group::2 MMA, 64 rows per CTA, the accumulator's two column halves in TMEM lanes 0-63 and
+    64-127). Remainders of 1, 64, 65, 128 and 129 rows, an empty group, a K tail and an N tail;
+    full compare against the oracle with the option on and off, each run twice."""
+    torch = _torch()
+    group_m, n, k = [1, 64, 0, 65, 128, 129, 256 + 100, 512 + 128], 8 * 97, 200
+    s = torch.cuda.current_stream().cuda_stream
+    up = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda()  # noqa: E731
+    if op == "forward":
+        x, w = orc.make_inputs(group_m, n, k, dtype)
+        ref, cols = orc.grouped_gemm_f32(x, w, group_m, dtype), n
+        xd, wd = up(x), up(w)
+    else:
+        dy, x, w = orc.make_grad_inputs(group_m, n, k, dtype)
+        ref, cols = orc.grouped_dgrad_f32(dy, w, group_m, dtype), k
+        dyd, wd = up(dy), up(w)
+    rows = sum(group_m)
+    for half in (1, 0):
+        out = torch.full((rows * cols + GUARD,), CANARY, dtype=torch.int16, device="cuda")
+        b = gg.B200Backend()
+        for key, val in {"variant": 0, "bn": bn, "split": 1, "half_tiles": half}.items():
+            b.set_option(key, val)
+        if op == "forward":
+            why = b.prepare(dtype, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s)
+        else:
+            why = b.prepare_grad(gg.OP_DGRAD, dtype, group_m, n, k, dy_ptr=dyd.data_ptr(), w_ptr=wd.data_ptr(),
+                                 dx_ptr=out.data_ptr(), stream=s)
+        if op == "dgrad" and why and "multiple of 64" in why:
+            continue  # a backward tile width must be a multiple of 64 per CTA
+        assert why == "", why
+        assert ("half-tiles" in b.detail()) == bool(half), b.detail()
+        for _ in range(2):
+            out[:rows * cols].fill_(0)
+            b.run(s)
+            assert b.device_status(s) == 0, b.detail()
+            res = out.cpu().numpy().view(np.uint16)
+            assert np.all(res[rows * cols:] == CANARY), (b.detail(), "store past the end of out")
+            bad, mx, first = orc.check16(res[:rows * cols].reshape(rows, cols), ref, dtype)
+            assert bad == 0, (b.detail(), bad, mx, divmod(first, cols) if first >= 0 else first)
+        b.release()
+
+
+def test_half_height_tiles_with_dynamic_dispatch_and_graph(gg, orc):
+    """Half-height tiles under dynamic dispatch on a capped grid (many waves), replayed from a
+    captured CUDA graph."""
+    torch = _torch()
+    group_m, n, k = [100, 700, 3, 0, 128, 1000, 60], 512, 384
+    x, w = orc.make_inputs(group_m, n, k, 0)
+    ref = orc.grouped_gemm_f32(x, w, group_m, 0)
+    xd, wd = upload(torch, x), upload(torch, w)
+    out = torch.zeros(sum(group_m) * n, dtype=torch.int16, device="cuda")
+    st = torch.cuda.Stream()
+    b = gg.B200Backend()
+    for key, val in {"variant": 0, "max_ctas": 6, "sched": 1, "split": 1}.items():
+        b.set_option(key, val)
+    assert b.prepare(0, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), st.cuda_stream) == ""
+    assert "half-tiles" in b.detail() and "dynamic" in b.detail(), b.detail()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for _ in range(2):
+            b.run(torch.cuda.current_stream().cuda_stream)
+    for _ in range(2):
+        out.zero_()
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        assert b.device_status(st.cuda_stream) == 0
+        assert orc.check16(out.cpu().numpy().view(np.uint16).reshape(-1, n), ref, 0)[0] == 0
