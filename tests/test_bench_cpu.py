@@ -89,8 +89,8 @@ def test_roofline_traffic_follows_the_shard_and_stays_under_hbm_peak():
                 r = bench.roofline(flops, alg, ms, peaks, "measured", caps, "test")
                 assert r["traffic"] is not None and r["traffic"] >= 0.99 * alg, (name, world, r)
                 assert r["hbm"]["traffic_gbs"] < r["hbm"]["peak_gbs"], (name, world, r["hbm"])
-                if world > 1 and name == "E":
-                    assert "scaled" in r["traffic_source"]
+                exact = any(c["algorithmic_bytes"] == alg for c in caps)
+                assert ("scaled" in r["traffic_source"]) == (not exact), (name, world, r["traffic_source"])
     # no capture: null traffic with a reason, never a number from another launch
     r = bench.roofline(1e12, 1e9, 1.0, peaks, "measured", [], "test")
     assert r["traffic"] is None and r["hbm"]["traffic_gbs"] is None and r["traffic_source"]
