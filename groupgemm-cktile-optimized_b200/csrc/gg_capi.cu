@@ -111,7 +111,8 @@ struct gg_handle {
     int opt_test_stall = 0;
     int opt_pdl = 1;
     int opt_store = -1;  // -1 auto, 0 = staging + TMA stores, 1 = direct stores
-    int opt_half = -1;   // -1 auto (= on where a group ends in a remainder of at most 128 rows), 0 off, 1 on
+    int opt_tail = -1;   // split launch for skewed routing: -1 auto, 0 off, 1 on
+    int opt_half = 0;    // 1 on (half-height last tiles where a group allows), 0 off (default), -1 = on
     int opt_sched = 0;  // -1 auto (dynamic for multi-wave launches of whole tiles), 0 static, 1 dynamic
 
     // prepared state
@@ -132,6 +133,15 @@ struct gg_handle {
     int op = 0;                      // gg::kOpForward / kOpDgrad / kOpWgrad
     CUtensorMap tmap_a{}, tmap_b{}, tmap_out{};
     CUtensorMap tmap_a_half{};  // A in 64-row boxes, for half-height pair tiles
+    // Second launch of a split launch: the one-CTA kernel over the groups' remainders of at most
+    // 128 rows (tmap_a / tmap_out are shared with the first launch).
+    struct {
+        bool active = false;
+        const void *fn = nullptr;
+        int grid = 0, smem = 0;
+        CUtensorMap tmap_b{};
+        gg::KernelParams params{};
+    } tail;
     gg::KernelParams params{};
     int grid = 0;
     const void *fn = nullptr;
@@ -226,6 +236,10 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < -1 || value > 1)
             return fail(h, GG_ERR_ARG, "store must be -1 (auto), 0 (TMA stores) or 1 (direct stores)");
         h->opt_store = int(value);
+    } else if (!std::strcmp(key, "tail_launch")) {
+        if (value < -1 || value > 1)
+            return fail(h, GG_ERR_ARG, "tail_launch must be -1 (auto), 0 (off) or 1 (on)");
+        h->opt_tail = int(value);
     } else if (!std::strcmp(key, "half_tiles")) {
         if (value < -1 || value > 1)
             return fail(h, GG_ERR_ARG, "half_tiles must be -1 (auto), 0 (off) or 1 (on)");
@@ -270,6 +284,7 @@ void gg_release(gg_handle *h) {
     h->ws_cap = 0;
     h->counters_cap = 0;
     h->meta_cap = 0;
+    h->tail.active = false;
     h->ready = false;
     h->detail.clear();
 }
@@ -463,20 +478,56 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     const Variant &v = variant_at(vi);
     const void *fn = v.fn[op][q.dtype];
 
-    // ---- group arguments: tile offsets (this tiling) and row (token) offsets ----
+    // ---- split launch for skewed routing ----
+    // A group whose last 256-row pair tile would hold at most 128 rows (a small expert, or the
+    // remainder of a larger one) wastes over half of that tile. With the 2-CTA variant chosen for
+    // forward / dgrad and whole tiles, such remainders go to a second launch of the one-CTA kernel
+    // (128-row tiles), and the pair kernel covers each group's other rows; automatic when at least
+    // 5% of the pair m-tiles are such remainders.
+    std::vector<int64_t> small(size_t(G), 0);
+    bool tail = false;
+    if (v.cg == 2 && op != gg::kOpWgrad && ch.splits <= 1 && ch.sk == 0 && h->opt_tail != 0) {
+        int64_t n_small = 0, n_mt = 0;
+        for (int g = 0; g < G; ++g) {
+            const int64_t rem = q.group_m[g] % 256;
+            if (rem > 0 && rem <= 128) {
+                small[size_t(g)] = rem;
+                ++n_small;
+            }
+            n_mt += (q.group_m[g] + 255) / 256;
+        }
+        tail = n_small > 0 && (h->opt_tail == 1 || 20 * n_small >= n_mt);
+        if (!tail)
+            std::fill(small.begin(), small.end(), 0);
+    }
+
+    // ---- group arguments: tile offsets (this tiling) and row (token) offsets; with a split launch
+    // also the rows each launch covers per group, then the tail launch's tables ----
     const int64_t tiles_n = (out_cols + bn - 1) / bn;
-    std::vector<int32_t> meta(2 * size_t(G + 1));
-    int64_t tiles = 0, rows = 0;
+    const size_t T1 = size_t(G + 1);  // entries of one offset table
+    std::vector<int32_t> meta(tail ? 6 * size_t(G) + 4 : 2 * T1);
+    int64_t tiles = 0, rows = 0, tail_tiles = 0;
     for (int g = 0; g < G; ++g) {
-        meta[g] = int32_t(tiles);
-        meta[G + 1 + g] = int32_t(rows);
-        tiles += (cm.group_m[g] + v.cluster_m - 1) / v.cluster_m * tiles_n;
+        meta[size_t(g)] = int32_t(tiles);
+        meta[T1 + size_t(g)] = int32_t(rows);
+        tiles += (cm.group_m[g] - small[size_t(g)] + v.cluster_m - 1) / v.cluster_m * tiles_n;
+        if (tail) {
+            meta[2 * T1 + size_t(g)] = int32_t(q.group_m[g] - small[size_t(g)]);              // pair rows
+            meta[2 * T1 + size_t(G) + size_t(g)] = int32_t(tail_tiles);                         // tail tile_off
+            meta[3 * T1 + size_t(G) + size_t(g)] = int32_t(rows + q.group_m[g] - small[size_t(g)]);  // tail row_off
+            meta[4 * T1 + size_t(G) + size_t(g)] = int32_t(small[size_t(g)]);                   // tail rows
+            tail_tiles += small[size_t(g)] > 0 ? tiles_n : 0;
+        }
         rows += q.group_m[g];
         if (tiles >= (int64_t(1) << 31))
             return refuse(h, why, why_len, "too many tiles");
     }
-    meta[G] = int32_t(tiles);
-    meta[2 * G + 1] = int32_t(rows);
+    meta[size_t(G)] = int32_t(tiles);
+    meta[T1 + size_t(G)] = int32_t(rows);
+    if (tail) {
+        meta[2 * T1 + 2 * size_t(G)] = int32_t(tail_tiles);
+        meta[3 * T1 + 2 * size_t(G)] = int32_t(rows);
+    }
     // Split-K form: every tile split, or (hybrid) only as many tiles as would form a partial last
     // wave; the split tiles' units run first, the whole tiles after them.
     // Stream-K instead: the first sk_tiles tiles' atoms dealt out evenly to every cluster.
@@ -531,7 +582,7 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     bool half_tiles = false;
     if (v.cg == 2 && op != gg::kOpWgrad && !partials && bn % 32 == 0 && h->opt_half != 0)
         for (int g = 0; g < G && !half_tiles; ++g)
-            half_tiles = (q.group_m[g] % 256) != 0 && (q.group_m[g] % 256) <= 128;
+            half_tiles = ((q.group_m[g] - small[size_t(g)]) % 256) != 0 && ((q.group_m[g] - small[size_t(g)]) % 256) <= 128;
 
     // ---- TMA descriptors ----
     const CUtensorMapDataType dt =
@@ -612,6 +663,7 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     kp = gg::KernelParams{};
     kp.tile_off = h->d_meta;
     kp.row_off = h->d_meta + (G + 1);
+    kp.row_cnt = tail ? h->d_meta + 2 * (G + 1) : nullptr;
     kp.out = q.out;
     kp.status = h->d_status;
     kp.gmaps = op == gg::kOpWgrad ? h->d_gmaps : nullptr;
@@ -641,6 +693,35 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     const bool dynamic = !partials && (h->opt_sched == 1 || (h->opt_sched < 0 && units * v.cg > h->grid));
     kp.tile_ctr = dynamic ? reinterpret_cast<int32_t *>(h->d_status) + 1 : nullptr;
 
+    // The tail launch: the one-CTA 128-row kernel over the remainders, same tile width, static
+    // schedule, whole tiles; its own weight map (each CTA loads all bn weight rows of a tile).
+    h->tail.active = false;
+    h->tail.tmap_b = CUtensorMap{};
+    if (tail && tail_tiles > 0) {
+        const Variant &tv = variant_at(1);
+        if (op == gg::kOpForward) {
+            if (encode_w(encode, &h->tail.tmap_b, dt, q.b, q.n, q.k, G, gg::kBK, uint32_t(bn)))
+                return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(w, tail launch) failed");
+        } else {
+            h->tail.tmap_b = h->tmap_b;  // dgrad: 64 x 64 MN-major boxes either way
+        }
+        GG_CUDA(h, cudaFuncSetAttribute(tv.fn[op][q.dtype], cudaFuncAttributeMaxDynamicSharedMemorySize, tv.smem));
+        gg::KernelParams &tp = h->tail.params;
+        tp = kp;
+        tp.tile_off = h->d_meta + 2 * (G + 1) + G;
+        tp.row_off = h->d_meta + 3 * (G + 1) + G;
+        tp.row_cnt = h->d_meta + 4 * (G + 1) + G;
+        tp.total_tiles = int32_t(tail_tiles);
+        tp.band = 16;
+        tp.tile_ctr = nullptr;
+        tp.half_tiles = 0;
+        tp.test_stall = 0;
+        h->tail.fn = tv.fn[op][q.dtype];
+        h->tail.smem = tv.smem;
+        h->tail.grid = int(std::min<int64_t>(num_sms, tail_tiles));
+        h->tail.active = true;
+    }
+
     GG_CUDA(h, cudaStreamSynchronize(stream));
 
     h->device = dev;
@@ -651,18 +732,22 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     h->fn = fn;
     h->smem = v.smem;
     h->cg = v.cg;
-    char form[64];
+    char form[160];
     if (sk_tiles > 0)
         std::snprintf(form, sizeof(form), "split=1 stream_k=%lld tiles(<=%d pieces)", (long long)sk_tiles, ch.splits);
     else
         std::snprintf(form, sizeof(form), "split=%d%s%s%s", ch.splits,
                       split_tiles > 0 && split_tiles < tiles ? "(last wave)" : "", dynamic ? " dynamic" : "",
                       half_tiles ? " half-tiles" : "");
-    char d[256];
-    std::snprintf(d, sizeof(d), "gg_sm100<%s%s%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld %s grid=%d band=%d%s",
+    char tail_form[96] = "";
+    if (h->tail.active)
+        std::snprintf(tail_form, sizeof(tail_form), " +tail gg_sm100 tile=128x%d cta_group=1 tiles=%lld grid=%d", bn,
+                      (long long)tail_tiles, h->tail.grid);
+    char d[384];
+    std::snprintf(d, sizeof(d), "gg_sm100<%s%s%s> tile=%dx%dx%d cta_group=%d stages=%d tiles=%lld %s grid=%d band=%d%s%s",
                   q.dtype == GG_BF16 ? "bf16" : "fp16", op == gg::kOpForward ? "" : ",", op == gg::kOpForward ? "" : op_name(op),
                   v.cluster_m, bn, gg::kBK * v.atoms, v.cg, v.stages_for(bn / v.cg), (long long)tiles, form, h->grid, band,
-                  raster ? "n" : "");
+                  raster ? "n" : "", tail_form);
     h->detail = d;
     h->ready = true;
     return GG_OK;
@@ -711,7 +796,7 @@ int gg_run(gg_handle *h, gg_stream_t stream) {
         return GG_ERR_ARG;
     if (!h->ready)
         return fail(h, GG_ERR_ARG, "gg_run before a successful gg_prepare");
-    if (h->params.total_tiles == 0)
+    if (h->params.total_tiles == 0 && !h->tail.active)
         return GG_OK;  // every group empty: nothing to write
     cudaLaunchConfig_t cfg{};
     cudaLaunchAttribute attr[2];
@@ -730,8 +815,19 @@ int gg_run(gg_handle *h, gg_stream_t stream) {
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = h->opt_pdl ? 2 : 1;
-    void *args[5] = {&h->tmap_a, &h->tmap_b, &h->tmap_out, &h->tmap_a_half, &h->params};
-    GG_CUDA(h, cudaLaunchKernelExC(&cfg, h->fn, args));
+    if (h->params.total_tiles > 0) {
+        void *args[5] = {&h->tmap_a, &h->tmap_b, &h->tmap_out, &h->tmap_a_half, &h->params};
+        GG_CUDA(h, cudaLaunchKernelExC(&cfg, h->fn, args));
+    }
+    if (h->tail.active) {
+        // split launch: the one-CTA kernel over the groups' remainders (rows disjoint from the first
+        // launch's), behind it in the stream
+        attr[0].val.clusterDim.x = 1;
+        cfg.gridDim = dim3(unsigned(h->tail.grid), 1, 1);
+        cfg.dynamicSmemBytes = size_t(h->tail.smem);
+        void *args[5] = {&h->tmap_a, &h->tail.tmap_b, &h->tmap_out, &h->tmap_a_half, &h->tail.params};
+        GG_CUDA(h, cudaLaunchKernelExC(&cfg, h->tail.fn, args));
+    }
     return GG_OK;
 }
 

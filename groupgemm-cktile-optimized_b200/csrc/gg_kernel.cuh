@@ -91,6 +91,9 @@ enum : int { kOpForward = 0, kOpDgrad = 1, kOpWgrad = 2 };
 struct KernelParams {
     const int32_t *tile_off;  // [G+1] first tile of each group (cluster tiles)
     const int32_t *row_off;   // [G+1] first row (token) of each group in x / dy / out / dx
+    const int32_t *row_cnt;   // null: group g has row_off[g+1] - row_off[g] rows; else [G] the rows this
+                              // launch covers from row_off[g] (a split launch: the pair kernel takes each
+                              // group's whole 256-row tiles, a one-CTA launch the remainders)
     void *out;
     uint32_t *status;
     const CUtensorMap *gmaps;  // wgrad: [2G] per-group maps (A = dy rows of g, B = x rows of g)
@@ -222,7 +225,7 @@ __host__ __device__ __forceinline__ TileCoord decode_tile(const KernelParams &p,
     tc.g = cursor;
     const int local = t - ld_table(&p.tile_off[tc.g]);
     const int r0 = ld_table(&p.row_off[tc.g]);
-    const int m = ld_table(&p.row_off[tc.g + 1]) - r0;
+    const int m = p.row_cnt ? ld_table(&p.row_cnt[tc.g]) : ld_table(&p.row_off[tc.g + 1]) - r0;
     if constexpr (kOp == kOpWgrad) {
         tc.rows = p.tile_rows;
         tc.out_row0 = tc.g * p.tile_rows;

@@ -51,7 +51,9 @@ def draw_case(rng):
     if rng.random() < 0.5:
         opts["sched"] = int(rng.integers(0, 2))  # static or dynamic tile dispatch (else automatic)
     if rng.random() < 0.3:
-        opts["half_tiles"] = 0  # otherwise automatic: half-height last tiles where a group allows
+        opts["half_tiles"] = int(rng.integers(0, 2))
+    if rng.random() < 0.5:
+        opts["tail_launch"] = int(rng.integers(0, 2))  # otherwise automatic (skewed remainders)
     return group_m, n, k, op, dtype, opts
 
 

@@ -623,7 +623,7 @@ def test_half_height_pair_tiles(gg, orc, dtype, bn, op):
     for half in (1, 0):
         out = torch.full((rows * cols + GUARD,), CANARY, dtype=torch.int16, device="cuda")
         b = gg.B200Backend()
-        for key, val in {"variant": 0, "bn": bn, "split": 1, "half_tiles": half}.items():
+        for key, val in {"variant": 0, "bn": bn, "split": 1, "half_tiles": half, "tail_launch": 0}.items():
             b.set_option(key, val)
         if op == "forward":
             why = b.prepare(dtype, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s)
@@ -656,7 +656,7 @@ def test_half_height_tiles_with_dynamic_dispatch_and_graph(gg, orc):
     out = torch.zeros(sum(group_m) * n, dtype=torch.int16, device="cuda")
     st = torch.cuda.Stream()
     b = gg.B200Backend()
-    for key, val in {"variant": 0, "max_ctas": 6, "sched": 1, "split": 1}.items():
+    for key, val in {"variant": 0, "max_ctas": 6, "sched": 1, "split": 1, "half_tiles": 1, "tail_launch": 0}.items():
         b.set_option(key, val)
     assert b.prepare(0, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), st.cuda_stream) == ""
     assert "half-tiles" in b.detail() and "dynamic" in b.detail(), b.detail()
@@ -671,3 +671,61 @@ def test_half_height_tiles_with_dynamic_dispatch_and_graph(gg, orc):
         torch.cuda.synchronize()
         assert b.device_status(st.cuda_stream) == 0
         assert orc.check16(out.cpu().numpy().view(np.uint16).reshape(-1, n), ref, 0)[0] == 0
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+@pytest.mark.parametrize("op", ["forward", "dgrad"])
+@pytest.mark.parametrize("group_m", [
+    [1, 64, 0, 65, 128, 129, 256 + 100, 512 + 128, 300],   # remainders of every kind
+    [100, 3, 128, 77, 0, 1],                              # every group small: the pair launch has no tiles
+])
+def test_split_launch_for_skewed_routing(gg, orc, dtype, op, group_m):
+    """With the 2-CTA variant, groups whose last pair tile would hold at most 128 rows hand those
+    rows to a second launch of the one-CTA kernel (tail_launch). Full compare against the oracle
+    with the split on and off, two runs each, and in a captured CUDA graph."""
+    torch = _torch()
+    n, k = 8 * 97, 200 if op == "forward" else 8 * 50
+    s = torch.cuda.current_stream().cuda_stream
+    up = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda()  # noqa: E731
+    if op == "forward":
+        x, w = orc.make_inputs(group_m, n, k, dtype)
+        ref, cols = orc.grouped_gemm_f32(x, w, group_m, dtype), n
+        xd, wd = up(x), up(w)
+    else:
+        dy, x, w = orc.make_grad_inputs(group_m, n, k, dtype)
+        ref, cols = orc.grouped_dgrad_f32(dy, w, group_m, dtype), k
+        dyd, wd = up(dy), up(w)
+    rows = sum(group_m)
+    for split in (1, 0):
+        out = torch.full((rows * cols + GUARD,), CANARY, dtype=torch.int16, device="cuda")
+        b = gg.B200Backend()
+        for key, val in {"variant": 0, "split": 1, "tail_launch": split, "bn": 256 if op == "dgrad" else 0}.items():
+            b.set_option(key, val)
+        if op == "forward":
+            why = b.prepare(dtype, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s)
+        else:
+            why = b.prepare_grad(gg.OP_DGRAD, dtype, group_m, n, k, dy_ptr=dyd.data_ptr(), w_ptr=wd.data_ptr(),
+                                 dx_ptr=out.data_ptr(), stream=s)
+        assert why == "", why
+        assert ("+tail" in b.detail()) == bool(split), b.detail()
+        for _ in range(2):
+            out[:rows * cols].fill_(0)
+            b.run(s)
+            assert b.device_status(s) == 0, b.detail()
+            res = out.cpu().numpy().view(np.uint16)
+            assert np.all(res[rows * cols:] == CANARY), (b.detail(), "store past the end of out")
+            bad, mx, first = orc.check16(res[:rows * cols].reshape(rows, cols), ref, dtype)
+            assert bad == 0, (b.detail(), bad, mx, divmod(first, cols) if first >= 0 else first)
+        if split:
+            st = torch.cuda.Stream()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                b.run(torch.cuda.current_stream().cuda_stream)
+            out[:rows * cols].fill_(0)
+            torch.cuda.synchronize()
+            g.replay()
+            torch.cuda.synchronize()
+            assert b.device_status(s) == 0
+            bad, _, _ = orc.check16(out.cpu().numpy().view(np.uint16)[:rows * cols].reshape(rows, cols), ref, dtype)
+            assert bad == 0, (b.detail(), "graph replay")
+        b.release()
