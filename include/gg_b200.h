@@ -110,7 +110,8 @@ int gg_prepare_grad(gg_handle *h, const gg_grad_problem *p, int32_t op, gg_strea
                     size_t why_len);
 
 /* Backend::run() (common/backend.hpp:67; ck_kernel/ck_grouped_gemm.cpp:140, :114-121). Timed:
- * enqueues exactly one kernel launch on `stream` and does not synchronise. */
+ * enqueues one grouped GEMM on `stream` and does not synchronise: one kernel launch, or two for
+ * a split launch ("tail_launch" below). */
 int gg_run(gg_handle *h, gg_stream_t stream);
 
 /* Backend::release() (common/backend.hpp:69; ck_kernel/ck_grouped_gemm.cpp:142-146): frees
@@ -155,11 +156,16 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
  *                finishes one, so tiles that share a weight panel stay in step all launch long.
  *                The counter is zero between launches, so launches of one handle must not overlap
  *                on the GPU (order them on one stream, as for any handle)
- *   "half_tiles" -1 auto (= on), 0 off, 1 on: with the 2-CTA variant (forward and dgrad, no
+ *   "tail_launch" -1 auto (default), 0 off, 1 on: with the 2-CTA variant (forward and dgrad, no
+ *                split-K or stream-K), the rows of each group's last 256-row tile, where they are at
+ *                most 128, go to a second launch of the one-CTA kernel (128-row tiles) right behind
+ *                the first in the stream; gg_run then enqueues two kernels. Automatic when at least
+ *                5% of the pair m-tiles are such remainders (skewed routing: many small experts)
+ *   "half_tiles" 0 off (default), 1 / -1 on: with the 2-CTA variant (forward and dgrad, no
  *                split-K or stream-K, a tile width that is a multiple of 32), a group whose last
  *                256-row tile holds at most 128 rows runs that tile half height (an M = 128 pair
- *                MMA, 64 rows per CTA, same tensor rate per row), so a small expert's remainder
- *                costs half a tile, not a padded whole one (skewed routing)
+ *                MMA, 64 rows per CTA). Measured slower than the split launch and than padding on
+ *                B200 (a half tile costs ~0.9 of a whole one), so it is off unless asked for
  *   "pdl"        1 (default) = launch with programmatic stream serialisation, so the launch and
  *                on-chip set-up overlap the previous kernel in the stream; 0 = plain launch
  *   "max_ctas"   cap on the persistent grid (0 = one CTA per SM)
