@@ -40,7 +40,8 @@ def main(out_path):
     be.run(s)
     assert be.device_status(s) == 0
     gathered = torch.empty(B * M, N, dtype=torch.int16, device="cuda")
-    dist.all_gather_into_tensor(gathered, out)
+    # NCCL has no 16-bit integer type: move the raw bits as bf16 (a bit-preserving view)
+    dist.all_gather_into_tensor(gathered.view(torch.bfloat16), out.view(torch.bfloat16))
     torch.cuda.synchronize()
     if rank == 0:
         whole = torch.zeros(B * M, N, dtype=torch.int16, device="cuda")

@@ -37,7 +37,7 @@ def test_sharded_outputs_all_gather_to_the_unsharded_result(tmp_path):
            f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(ROOT, "tests", "ep_allgather_worker.py"), str(out)]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
-    assert r.returncode == 0, (r.stdout[-3000:], r.stderr[-3000:])
+    assert r.returncode == 0, (r.stdout[-2000:], r.stderr[-6000:])
     res = json.loads(out.read_text())
     assert res["world"] == world
     assert res["bitwise_equal_to_unsharded"], res
