@@ -999,7 +999,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // chunk by chunk. The other pieces' blocks stream in (chunk, piece) order through a
                 // ring of kPrefetch register buffers, so that many L2 reads are in flight at once;
                 // the ring is indexed at compile time (block b sits in buffer b % kPrefetch).
-                constexpr int kPrefetch = 2;
+                constexpr int kPrefetch = 3;
                 const int others = nsplit - 1;
                 const int nb = nch * others;
                 auto load_blk = [&](int b, float4 (&dst)[8]) {
@@ -1062,28 +1062,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             } else {
-                // Direct stores, two 32-column chunks per TMEM wait: both loads are in flight
-                // before the wait, then both chunks are converted and stored.
 #pragma unroll 1
-                for (int c = c_tma; store_out && c < nch; c += 2) {
-                    uint32_t rr[2][32];
-                    const bool two = c + 1 < nch;
-                    ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), rr[0]);
-                    if (two)
-                        ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + 1) * 32), rr[1]);
-                    ptx::tmem_wait_ld(rr[0]);
-                    ptx::tmem_tie(rr[1]);
+                for (int c = c_tma; store_out && c < nch; ++c) {
+                    uint32_t r[32];
+                    ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
+                    ptx::tmem_wait_ld(r);
+                    if (zero_tile) {
 #pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        if (hh == 1 && !two)
-                            break;
-                        if (zero_tile) {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                rr[hh][j] = 0u;
-                        }
-                        store_chunk(c + hh, rr[hh]);
+                        for (int j = 0; j < 32; ++j)
+                            r[j] = 0u;
                     }
+                    store_chunk(c, r);
                 }
             }
             ptx::tc_fence_before();
