@@ -999,7 +999,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // chunk by chunk. The other pieces' blocks stream in (chunk, piece) order through a
                 // ring of kPrefetch register buffers, so that many L2 reads are in flight at once;
                 // the ring is indexed at compile time (block b sits in buffer b % kPrefetch).
-                constexpr int kPrefetch = 3;
+                constexpr int kPrefetch = 2;
                 const int others = nsplit - 1;
                 const int nb = nch * others;
                 auto load_blk = [&](int b, float4 (&dst)[8]) {
