@@ -17,6 +17,9 @@ from typing import Sequence
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libgg_b200.so")
+# The same C ABI with the kernel's bounds checks compiled in (-DGG_DEBUG): load it with
+# load_library(DEBUG_LIB_PATH) into a module of its own (see tests/test_gpu_debug_build.py).
+DEBUG_LIB_PATH = os.path.join(HERE, "lib", "libgg_b200_debug.so")
 
 BF16, FP16 = 0, 1
 DTYPES = {"bf16": BF16, "fp16": FP16}

@@ -2,6 +2,7 @@
 
 Outputs, in-tree so they travel with the repository snapshot:
   lib/libgg_b200.so   C ABI of include/gg_b200.h (static CUDA runtime)
+  lib/libgg_b200_debug.so  the same with the kernel's bounds checks (-DGG_DEBUG)
   lib/gg_bench        C++ shapes-CSV -> results-CSV benchmark (bench_main contract)
 
 Usage: python build.py [--force] [--resource-usage]
@@ -31,8 +32,15 @@ COMMON = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-I" + INCLUDE, "-I" + CSRC]
 TARGETS = {
     "libgg_b200.so": {
         "srcs": ["gg_capi.cu"],
-        "deps": ["gg_capi.cu", "gg_kernel.cuh", "gg_ptx.cuh"],
+        "deps": ["gg_capi.cu", "gg_kernel.cuh", "gg_ptx.cuh", "gg_sched.h"],
         "flags": ["-Xcompiler", "-fPIC", "-shared"],
+    },
+    # the same library with the kernel's bounds checks compiled in (-DGG_DEBUG): a failed check
+    # records its site in the device status word and skips the access
+    "libgg_b200_debug.so": {
+        "srcs": ["gg_capi.cu"],
+        "deps": ["gg_capi.cu", "gg_kernel.cuh", "gg_ptx.cuh", "gg_sched.h"],
+        "flags": ["-Xcompiler", "-fPIC", "-shared", "-DGG_DEBUG"],
     },
     "gg_bench": {
         "srcs": ["gg_bench_main.cu", "gg_cublas_backends.cpp", "gg_capi.cu"],

@@ -109,6 +109,7 @@ struct gg_handle {
     int opt_max_ctas = 0;
     int64_t opt_timeout_ms = 2000;
     int opt_test_stall = 0;
+    int opt_test_bounds = 0;  // test only: declare the output one row short to the debug build's checks
     int opt_pdl = 1;
     int opt_store = -1;  // -1 auto, 0 = staging + TMA stores, 1 = direct stores
     int opt_tail = -1;   // split launch for skewed routing: -1 auto, 0 off, 1 on
@@ -252,6 +253,10 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value != 0 && value != 1)
             return fail(h, GG_ERR_ARG, "pdl must be 0 or 1");
         h->opt_pdl = int(value);
+    } else if (!std::strcmp(key, "test_bounds")) {
+        if (value != 0 && value != 1)
+            return fail(h, GG_ERR_ARG, "test_bounds must be 0 or 1");
+        h->opt_test_bounds = int(value);
     } else if (!std::strcmp(key, "test_stall")) {
         if (value != 0 && value != 1)
             return fail(h, GG_ERR_ARG, "test_stall must be 0 or 1");
@@ -686,6 +691,9 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     kp.store_min_atoms = h->opt_store == 0 ? (1 << 30) : h->opt_store == 1 ? 0 : 16;
     kp.test_stall = h->opt_test_stall;
     kp.half_tiles = half_tiles && total_m > 0 ? 1 : 0;
+    kp.out_rows = int32_t(op == gg::kOpWgrad ? int64_t(G) * q.n : total_m) - h->opt_test_bounds;
+    kp.ws_float4s = partials ? int64_t(h->ws_cap / 16) : 0;
+    kp.ctr_entries = partials ? int32_t(h->counters_cap / sizeof(int32_t)) : 0;
     kp.timeout_ns = uint64_t(h->opt_timeout_ms) * 1000000ull;
     // Dynamic tile dispatch (whole tiles only): clusters take the next tile from a counter as they
     // finish one, so tiles that share a weight panel run at the same time all through the launch
@@ -846,7 +854,8 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status) {
         // an aborted launch can leave split-K arrival counts behind: clear them
         if (h->d_counters)
             GG_CUDA(h, cudaMemset(h->d_counters, 0, h->counters_cap));
-        return fail(h, GG_ERR_DEVICE, "kernel bounded wait timed out: status 0x%x", *status);
+        return fail(h, GG_ERR_DEVICE, "%s: status 0x%x",
+                    (*status & gg::kStatusBounds) ? "debug bounds check failed" : "kernel bounded wait timed out", *status);
     }
     return GG_OK;
 }
@@ -1100,6 +1109,7 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
     kp.total_tiles = int32_t(tiles);
     kp.band = v.cg == 2 ? 8 : 16;
     kp.store_min_atoms = 16;  // the same epilogue store policy as gg_run's default
+    kp.out_rows = int32_t(total_m);
     kp.timeout_ns = 2000ull * 1000000ull;
 
     const int slots = v.cg == 2 ? 2 * d->clusters_v0 : d->num_sms;
@@ -1136,7 +1146,8 @@ extern "C" int gg_run_noalloc(const gg_problem *p, gg_stream_t stream, uint32_t 
         if (st != 0) {
             if ((e = cudaMemset(d_status, 0, sizeof(uint32_t))) != cudaSuccess)
                 return cuda_fail("cudaMemset(status)", e);
-            std::snprintf(msg, sizeof(msg), "kernel bounded wait timed out: status 0x%x", st);
+            std::snprintf(msg, sizeof(msg), "%s: status 0x%x",
+                          (st & gg::kStatusBounds) ? "debug bounds check failed" : "kernel bounded wait timed out", st);
             copy_msg(why, why_len, msg);
             return GG_ERR_DEVICE;
         }

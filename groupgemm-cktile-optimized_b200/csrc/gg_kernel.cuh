@@ -77,9 +77,11 @@ constexpr int kBK = 64;        // K per swizzle atom: one 128-byte row of 16-bit
 constexpr int kUmmaK = 16;     // K per tcgen05.mma (kind::f16)
 constexpr int kSmemBudget = 200 * 1024;
 
-// Status word values (0 = ok). Timeouts encode role (bits 8-11) and barrier (bits 0-7).
+// Status word values (0 = ok). Timeouts encode role (bits 8-11) and barrier (bits 0-7); a failed
+// check of the bounds-checked debug build (GG_DEBUG) encodes the check's site in bits 0-7.
 enum : uint32_t {
     kStatusTimeout = 0x1000u,
+    kStatusBounds = 0x2000u,
     kRoleProducer = 1u << 8,
     kRoleMma = 2u << 8,
     kRoleEpilogue = 3u << 8,
@@ -124,8 +126,20 @@ struct KernelParams {
     int32_t *tile_ctr;    // non-null: dynamic tile dispatch (whole tiles only: splits <= 1, no
                           // stream-K). Cluster c takes tile c first, then tile C + atomicAdd(tile_ctr, 1)
                           // until past the last tile; 0 between launches (the last fetch resets it)
+    int32_t out_rows;     // rows of the output tensor (sum(M), or G * N for wgrad): debug checks
+    int64_t ws_float4s;   // float4 entries of the split-K / stream-K workspace: debug checks
+    int32_t ctr_entries;  // entries of the arrival-counter array: debug checks
     uint64_t timeout_ns;
 };
+
+// Bounds-checked debug build (-DGG_DEBUG, lib/libgg_b200_debug.so): GG_CHECK(cond, site) records
+// kStatusBounds | site in the status word (the first failure wins) and yields false, so the guarded
+// access is skipped; gg_device_status reports it. Nothing traps. In the release build it is true.
+#ifdef GG_DEBUG
+#define GG_CHECK(cond, site) ((cond) ? true : (atomicCAS(p.status, 0u, ::gg::kStatusBounds | uint32_t(site)), false))
+#else
+#define GG_CHECK(cond, site) true
+#endif
 
 template <typename T> struct Fmt;
 template <> struct Fmt<__nv_bfloat16> {
@@ -626,6 +640,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else {
                     tc = decode_tile<C::kClusterM, kOp>(p, un.t, cursor);
                 }
+                GG_CHECK(tc.g >= 0 && tc.g < p.group_num && tc.mt >= 0 && tc.nt >= 0 && tc.nt < p.tiles_n &&
+                             tc.mt * C::kClusterM < max(tc.rows, 1), 1);
                 const int atom0 = kOp == kOpWgrad ? 0 : un.atom0;
                 const int atom1 = kOp == kOpWgrad ? tc.red_atoms : un.atom1;
                 const int num_ks = (atom1 - atom0 + kAtoms - 1) / kAtoms;
@@ -848,6 +864,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int split = un.piece;
             const int nsplit = un.npieces;
             const TileCoord tc = decode_tile<C::kClusterM, kOp>(p, t, cursor);
+            GG_CHECK(tc.g >= 0 && tc.g < p.group_num && tc.mt >= 0 && tc.nt >= 0 && tc.nt < p.tiles_n &&
+                         t >= 0 && t < p.total_tiles, 1);
             const int acc = int(tl & 1u);
             const uint32_t acc_ph = (tl >> 1) & 1u;
             if (!wait_warp(tfull_bar(acc), acc_ph, ab, kStatusTimeout | kRoleEpilogue | uint32_t(acc)))
@@ -886,6 +904,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // fp32 fragment of one tcgen05.ld in lane order (float4 j of lane l at j * 32 + l),
                 // so every warp access is 512 contiguous bytes.
                 int32_t *ctr = p.counters + (int64_t(t) * kCG + int(cta_rank)) * 4 + q;
+                if (!GG_CHECK((int64_t(t) * kCG + int(cta_rank)) * 4 + q < p.ctr_entries, 5))
+                    break;
                 const bool fixed_summer = p.sk_tiles > 0 && split == 0;
                 if (!fixed_summer) {
                     float4 *wsw = reinterpret_cast<float4 *>(p.ws) + ws_warp + (int64_t(split) * nch) * 256 + lane;
@@ -896,6 +916,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ptx::tmem_wait_ld(r);
 #pragma unroll
                         for (int j = 0; j < 8; ++j)
+                            if (GG_CHECK(ws_warp + (int64_t(split) * nch + c) * 256 + lane + j * 32 < p.ws_float4s, 4))
                             __stcg(wsw + c * 256 + j * 32,
                                    make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
                                                __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
@@ -960,8 +981,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ptx::fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA engine
                 __syncwarp();
                 if (lane == 0) {
-                    ptx::tma_store_2d(&tmap_out, buf, tc.nt * bn + c * 32,
-                                      g_row0 + tc.mt * C::kClusterM + int(cta_rank) * kBM + q * 32, store_policy);
+                    const int sx = tc.nt * bn + c * 32, sy = g_row0 + tc.mt * C::kClusterM + int(cta_rank) * kBM + q * 32;
+                    if (GG_CHECK(sx >= 0 && sx < p.n && (sx & 7) == 0 && sy >= 0 && sy + 32 <= p.out_rows, 3))
+                        ptx::tma_store_2d(&tmap_out, buf, sx, sy, store_policy);
                     ptx::bulk_commit_group();
                 }
                 out_buf ^= 1;
@@ -974,6 +996,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!row_ok)
                     return;
                 const int col = col0 + c * 32;
+                if (!GG_CHECK(grow >= 0 && grow < p.out_rows && col >= 0 && (col & 7) == 0, 2))
+                    return;
                 uint32_t h[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
@@ -981,13 +1005,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
                     T *dst = orow + col + hh * 16;
-                    if (col + hh * 16 + 16 <= col_end && (reinterpret_cast<uintptr_t>(dst) & 31u) == 0) {
+                    if (col + hh * 16 + 16 <= col_end && (reinterpret_cast<uintptr_t>(dst) & 31u) == 0 &&
+                        GG_CHECK(col + hh * 16 + 16 <= p.n, 2)) {
                         ptx::st_cs_v8(dst, h[8 * hh], h[8 * hh + 1], h[8 * hh + 2], h[8 * hh + 3], h[8 * hh + 4],
                                       h[8 * hh + 5], h[8 * hh + 6], h[8 * hh + 7]);
                     } else {
 #pragma unroll
                         for (int j = 0; j < 2; ++j)
-                            if (col + hh * 16 + j * 8 < col_end)
+                            if (col + hh * 16 + j * 8 < col_end && GG_CHECK(col + hh * 16 + j * 8 + 8 <= p.n, 2))
                                 __stcs(reinterpret_cast<uint4 *>(dst + j * 8),
                                        make_uint4(h[8 * hh + 4 * j], h[8 * hh + 4 * j + 1], h[8 * hh + 4 * j + 2],
                                                   h[8 * hh + 4 * j + 3]));
@@ -1009,7 +1034,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float4 *src = reinterpret_cast<const float4 *>(p.ws) + ws_warp + (int64_t(s2) * nch + c) * 256 + lane;
 #pragma unroll
                     for (int j = 0; j < 8; ++j)
-                        dst[j] = __ldcg(src + j * 32);
+                        dst[j] = GG_CHECK(ws_warp + (int64_t(s2) * nch + c) * 256 + lane + j * 32 < p.ws_float4s, 4)
+                                     ? __ldcg(src + j * 32) : make_float4(0.f, 0.f, 0.f, 0.f);
                 };
                 float4 pf[kPrefetch][8];
 #pragma unroll

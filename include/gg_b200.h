@@ -127,7 +127,9 @@ const char *gg_last_error(const gg_handle *h);
 
 /* Synchronises `stream`, then reads and clears the kernel's device status word: 0 when every
  * launch since the last read finished normally, otherwise the first bounded-wait timeout code
- * (0x1000 | role << 8 | barrier). The outputs of every launch since the last read are then
+ * (0x1000 | role << 8 | barrier) or, in the bounds-checked debug build, the first failed check
+ * (0x2000 | site: 1 tile decode, 2 direct store, 3 TMA store box, 4 split-K workspace,
+ * 5 arrival counter; the checked access was skipped). The outputs of every launch since the last read are then
  * unreliable (an aborted launch stops part-way and can leave the dynamic-dispatch tile counter
  * and split-K arrival counts behind; this call resets them, so later launches are sound again).
  * No counterpart in the reference, whose kernel cannot time out (its only device-side guard is
@@ -170,6 +172,10 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
  *                on-chip set-up overlap the previous kernel in the stream; 0 = plain launch
  *   "max_ctas"   cap on the persistent grid (0 = one CTA per SM)
  *   "timeout_ms" bounded-wait limit inside the kernel (default 2000)
+ *   "test_bounds" test only: 1 = the kernel is told the output has one row fewer than it has, so
+ *                the bounds-checked debug build (lib/libgg_b200_debug.so, -DGG_DEBUG) finds the last
+ *                row's stores out of bounds, skips them and reports 0x2002 in the status word (the
+ *                release build has no checks and stores every row); used to test the checks
  *   "test_stall" test only: 1 = the kernel never loads the first stage of its first CTA (pair),
  *                so that wait runs out after timeout_ms and gg_device_status() reports it;
  *                used to test failure detection without faulting the GPU

@@ -27,6 +27,15 @@ def test_library_exports_every_declared_symbol(gg):
         assert n in gg.SIGNATURES, f"{n} has no ctypes signature"
 
 
+def test_debug_library_exports_the_same_symbols(gg):
+    """The bounds-checked debug build (-DGG_DEBUG) is the same C ABI."""
+    path = os.path.join(os.path.dirname(gg.LIB_PATH), "libgg_b200_debug.so")
+    assert os.path.exists(path), "build it with groupgemm-cktile-optimized_b200/build.py"
+    lib = ctypes.CDLL(path)
+    for n in declared_functions():
+        assert hasattr(lib, n), n
+
+
 def test_abi_version_and_name(gg):
     lib = gg.load_library()
     assert lib.gg_abi_version() == 1
@@ -68,11 +77,11 @@ def test_set_option(gg):
                      ("pdl", 0), ("pdl", 1), ("store", -1), ("store", 0), ("store", 1), ("stream_k", -1),
                      ("stream_k", 0), ("stream_k", 1), ("stream_k", 2), ("bn", 240), ("bn", 16), ("bn", 0),
                      ("sched", -1), ("sched", 0), ("sched", 1), ("half_tiles", -1), ("half_tiles", 0), ("half_tiles", 1),
-                     ("tail_launch", -1), ("tail_launch", 0), ("tail_launch", 1)):
+                     ("tail_launch", -1), ("tail_launch", 0), ("tail_launch", 1), ("test_bounds", 0), ("test_bounds", 1)):
         b.set_option(key, val)
     for key, val in (("variant", 7), ("band", -1), ("timeout_ms", 0), ("test_stall", 2), ("bn", 100), ("bn", 288), ("split", 9),
                      ("split_tail", 2), ("raster", 2), ("pdl", 3), ("store", 2), ("bogus", 1), ("bn", 24), ("bn", 8),
-                     ("stream_k", 3), ("stream_k", -2), ("sched", 2), ("sched", -2), ("half_tiles", 2), ("tail_launch", 2)):
+                     ("stream_k", 3), ("stream_k", -2), ("sched", 2), ("sched", -2), ("half_tiles", 2), ("tail_launch", 2), ("test_bounds", 2)):
         with pytest.raises(gg.GGError):
             b.set_option(key, val)
 
