@@ -981,8 +981,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ptx::fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA engine
                 __syncwarp();
                 if (lane == 0) {
+                    // a box that starts past the last column (the N tail of a tile) holds nothing to store
                     const int sx = tc.nt * bn + c * 32, sy = g_row0 + tc.mt * C::kClusterM + int(cta_rank) * kBM + q * 32;
-                    if (GG_CHECK(sx >= 0 && sx < p.n && (sx & 7) == 0 && sy >= 0 && sy + 32 <= p.out_rows, 3))
+                    if (sx < p.n && GG_CHECK(sx >= 0 && (sx & 7) == 0 && sy >= 0 && sy + 32 <= p.out_rows, 3))
                         ptx::tma_store_2d(&tmap_out, buf, sx, sy, store_policy);
                     ptx::bulk_commit_group();
                 }
