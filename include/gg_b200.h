@@ -152,12 +152,13 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
  *                refused with "split" > 1, for wgrad, and where the tiling has no partial wave)
  *   "store"      -1 auto (direct stores from registers for tiles with >= 16 K atoms, staging +
  *                TMA stores for shorter ones), 0 = always TMA stores, 1 = always direct stores
- *   "sched"      -1 auto (dynamic for launches of whole tiles with more tiles than CTAs / pairs),
- *                0 = static round-robin (cluster c runs tiles c, c + C, ...), 1 = dynamic dispatch:
- *                a cluster takes its next tile from a counter in the handle's device memory as it
- *                finishes one, so tiles that share a weight panel stay in step all launch long.
- *                The counter is zero between launches, so launches of one handle must not overlap
- *                on the GPU (order them on one stream, as for any handle)
+ *   "sched"      0 (default) = static round-robin (cluster c runs tiles c, c + C, ...), 1 = dynamic
+ *                dispatch: a cluster takes its next tile from a counter in the handle's device
+ *                memory as it finishes one, so tiles that share a weight panel stay in step all
+ *                launch long (fewer DRAM re-reads, but measured slower at the power cap), -1 =
+ *                dynamic for launches of whole tiles with more tiles than CTAs / pairs. The counter
+ *                is zero between launches, so launches of one handle must not overlap on the GPU
+ *                (order them on one stream, as for any handle)
  *   "tail_launch" -1 auto (default), 0 off, 1 on: with the 2-CTA variant (forward and dgrad, no
  *                split-K or stream-K), the rows of each group's last 256-row tile, where they are at
  *                most 128, go to a second launch of the one-CTA kernel (128-row tiles) right behind
