@@ -113,6 +113,8 @@ struct gg_handle {
     int opt_pdl = 1;
     int opt_store = -1;  // -1 auto, 0 = staging + TMA stores, 1 = direct stores
     int opt_tail = -1;   // split launch for skewed routing: -1 auto, 0 off, 1 on
+    int opt_chunks = 1;  // wgrad: 3-D chunk views for the MN-major operand loads where the shape allows
+    int opt_order = 0;  // planned tile order (wgrad with store-bound and tensor-bound groups): -1 auto, 0 off, 1 on
     int opt_half = 0;    // 1 on (half-height last tiles where a group allows), 0 off (default), -1 = on
     int opt_sched = 0;  // -1 auto (dynamic for multi-wave launches of whole tiles), 0 static, 1 dynamic
 
@@ -129,6 +131,8 @@ struct gg_handle {
     size_t ws_cap = 0;      // bytes
     int32_t *d_counters = nullptr;
     size_t counters_cap = 0;  // bytes
+    int32_t *d_tiles = nullptr;      // planned tile order: (group, mt << 16 | nt) per tile
+    size_t tiles_cap = 0;            // int32 entries
     CUtensorMap *d_gmaps = nullptr;  // wgrad: per-group tensor maps
     size_t gmaps_cap = 0;            // maps
     int op = 0;                      // gg::kOpForward / kOpDgrad / kOpWgrad
@@ -237,6 +241,14 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < -1 || value > 1)
             return fail(h, GG_ERR_ARG, "store must be -1 (auto), 0 (TMA stores) or 1 (direct stores)");
         h->opt_store = int(value);
+    } else if (!std::strcmp(key, "tma_chunks")) {
+        if (value < 0 || value > 1)
+            return fail(h, GG_ERR_ARG, "tma_chunks must be 0 (one 2-D box per 64-column chunk) or 1");
+        h->opt_chunks = int(value);
+    } else if (!std::strcmp(key, "tile_order")) {
+        if (value < -1 || value > 1)
+            return fail(h, GG_ERR_ARG, "tile_order must be -1 (auto), 0 (group order) or 1 (interleaved)");
+        h->opt_order = int(value);
     } else if (!std::strcmp(key, "tail_launch")) {
         if (value < -1 || value > 1)
             return fail(h, GG_ERR_ARG, "tail_launch must be -1 (auto), 0 (off) or 1 (on)");
@@ -280,6 +292,10 @@ void gg_release(gg_handle *h) {
         cudaFree(h->d_counters);
     if (h->d_gmaps)
         cudaFree(h->d_gmaps);
+    if (h->d_tiles)
+        cudaFree(h->d_tiles);
+    h->d_tiles = nullptr;
+    h->tiles_cap = 0;
     h->d_gmaps = nullptr;
     h->gmaps_cap = 0;
     h->d_meta = nullptr;
@@ -348,6 +364,20 @@ int encode_w(EncodeTiledFn encode, CUtensorMap *m, CUtensorMapDataType dt, const
     const cuuint32_t box[3] = {box_k, box_n, 1};
     const cuuint32_t estride[3] = {1, 1, 1};
     return int(encode(m, dt, 3, const_cast<void *>(w), dim, stride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
+}
+
+// A row-major [rows, cols] operand read MN-major (cols % 64 == 0) as a 3-D view: 64 columns, rows,
+// cols / 64 chunks 128 bytes apart. One box (64 x box_rows x chunks) lands in shared memory as
+// `chunks` consecutive 64 x box_rows boxes with the same 128-byte swizzle, so it replaces that many
+// 2-D box loads; every address it reads stays inside its row (column c * 64 + i < cols).
+int encode_mn_chunks(EncodeTiledFn encode, CUtensorMap *m, CUtensorMapDataType dt, const void *base, int64_t cols,
+                     int64_t rows, uint32_t box_rows, uint32_t chunks) {
+    const cuuint64_t dim[3] = {64, cuuint64_t(rows), cuuint64_t(cols / 64)};
+    const cuuint64_t stride[2] = {cuuint64_t(cols) * 2, 128};
+    const cuuint32_t box[3] = {64, box_rows, chunks};
+    const cuuint32_t estride[3] = {1, 1, 1};
+    return int(encode(m, dt, 3, const_cast<void *>(base), dim, stride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
 }
 
@@ -598,6 +628,7 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     h->tmap_b = CUtensorMap{};
     h->tmap_out = CUtensorMap{};
     std::vector<CUtensorMap> gmaps;
+    int mn_chunks = 0;
     if (op == gg::kOpForward && total_m > 0) {
         if (encode_2d(encode, &h->tmap_a, dt, q.a, q.k, total_m, gg::kBK, gg::kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
             return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed");
@@ -622,7 +653,10 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
             return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(dx) failed");
     } else if (op == gg::kOpWgrad) {
         // Per group: dy rows and x rows of the group's tokens, each bounded by the group so that the
-        // token tail reads zeros; 64 x 64 MN-major boxes. An empty group's maps are never read.
+        // token tail reads zeros; 64 x 64 MN-major boxes, or (N, resp. K, a multiple of 64) the 3-D
+        // chunk view that loads a CTA's 64-column chunks of an atom in one box. An empty group's
+        // maps are never read.
+        mn_chunks = h->opt_chunks != 0 ? (q.n % 64 == 0 ? 1 : 0) | (q.k % 64 == 0 ? 2 : 0) : 0;
         gmaps.assign(2 * size_t(G), CUtensorMap{});
         int64_t r0 = 0;
         for (int g = 0; g < G; ++g) {
@@ -630,8 +664,13 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
             if (m > 0) {
                 const char *dy = static_cast<const char *>(q.a) + r0 * q.n * 2;
                 const char *x = static_cast<const char *>(q.b) + r0 * q.k * 2;
-                if (encode_2d(encode, &gmaps[2 * g], dt, dy, q.n, m, 64, gg::kBK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B) ||
-                    encode_2d(encode, &gmaps[2 * g + 1], dt, x, q.k, m, 64, gg::kBK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+                const int ea = (mn_chunks & 1)
+                                   ? encode_mn_chunks(encode, &gmaps[2 * g], dt, dy, q.n, m, gg::kBK, uint32_t(gg::kBM / 64))
+                                   : encode_2d(encode, &gmaps[2 * g], dt, dy, q.n, m, 64, gg::kBK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+                const int eb = (mn_chunks & 2)
+                                   ? encode_mn_chunks(encode, &gmaps[2 * g + 1], dt, x, q.k, m, gg::kBK, b_box / 64)
+                                   : encode_2d(encode, &gmaps[2 * g + 1], dt, x, q.k, m, 64, gg::kBK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+                if (ea || eb)
                     return fail(h, GG_ERR_CUDA, "cuTensorMapEncodeTiled(group %d) failed", g);
             }
             r0 += m;
@@ -691,13 +730,64 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     kp.store_min_atoms = h->opt_store == 0 ? (1 << 30) : h->opt_store == 1 ? 0 : 16;
     kp.test_stall = h->opt_test_stall;
     kp.half_tiles = half_tiles && total_m > 0 ? 1 : 0;
+    kp.mn_chunks = mn_chunks;
     kp.out_rows = int32_t(op == gg::kOpWgrad ? int64_t(G) * q.n : total_m) - h->opt_test_bounds;
     kp.ws_float4s = partials ? int64_t(h->ws_cap / 16) : 0;
     kp.ctr_entries = partials ? int32_t(h->counters_cap / sizeof(int32_t)) : 0;
     kp.timeout_ns = uint64_t(h->opt_timeout_ms) * 1000000ull;
+    // Planned tile order (wgrad under skewed routing): an expert with few tokens has a short
+    // reduction, so its tiles are bound by their stores (a whole tile of output each), a large
+    // expert's by the tensor pipe. In group order the two kinds run as separate phases; the
+    // interleaved order (gg::interleave_tiles) with dynamic dispatch lets them overlap. Estimates
+    // per tile: bn/2 cycles per MMA (the tensor rate), ~11 bn cycles for the epilogue's stores.
+    bool planned = false;
+    if (op == gg::kOpWgrad && !partials && h->opt_order != 0 && tiles > 0) {
+        std::vector<double> cost(size_t(G), 0.0);
+        std::vector<char> store_bound(size_t(G), 0);
+        double work[2] = {0, 0};
+        const double epi = 11.0 * bn;
+        for (int g = 0; g < G; ++g) {
+            const double mma = double((q.group_m[g] + gg::kBK - 1) / gg::kBK) * 4.0 * 0.5 * bn;
+            cost[size_t(g)] = std::max(mma, epi);
+            store_bound[size_t(g)] = mma < epi ? 1 : 0;
+            work[store_bound[size_t(g)]] += cost[size_t(g)] * double(meta[size_t(g) + 1] - meta[size_t(g)]);
+        }
+        const double all = work[0] + work[1];
+        planned = h->opt_order == 1 || (work[0] > 0.05 * all && work[1] > 0.05 * all);
+        if (planned) {
+            // the tiles in group order, from the kernel's own decode over the host tables
+            gg::KernelParams hp = kp;
+            hp.tile_off = meta.data();
+            hp.row_off = meta.data() + (G + 1);
+            hp.row_cnt = nullptr;
+            hp.tile_list = nullptr;
+            std::vector<int32_t> natural(2 * size_t(tiles)), order;
+            int cursor = 0;
+            for (int64_t t = 0; t < tiles; ++t) {
+                const gg::TileCoord tc = v.cluster_m == 256 ? gg::decode_tile<256, gg::kOpWgrad>(hp, int(t), cursor)
+                                                            : gg::decode_tile<128, gg::kOpWgrad>(hp, int(t), cursor);
+                natural[2 * size_t(t)] = tc.g;
+                natural[2 * size_t(t) + 1] = (tc.mt << 16) | tc.nt;
+            }
+            gg::interleave_tiles(natural, cost, store_bound, order);
+            if (h->tiles_cap < order.size()) {
+                if (h->d_tiles)
+                    cudaFree(h->d_tiles);
+                h->d_tiles = nullptr;
+                h->tiles_cap = 0;
+                GG_CUDA(h, cudaMalloc(&h->d_tiles, order.size() * sizeof(int32_t)));
+                h->tiles_cap = order.size();
+            }
+            GG_CUDA(h, cudaMemcpyAsync(h->d_tiles, order.data(), order.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                       stream));
+            GG_CUDA(h, cudaStreamSynchronize(stream));  // `order` is a host temporary
+        }
+    }
+    kp.tile_list = planned ? h->d_tiles : nullptr;
     // Dynamic tile dispatch (whole tiles only): clusters take the next tile from a counter as they
     // finish one, so tiles that share a weight panel run at the same time all through the launch
-    // (a static round-robin lets clusters drift apart); automatic for launches of more than one wave.
+    // (a static round-robin lets clusters drift apart); automatic for launches of more than one
+    // wave. A planned tile order is dealt out either way.
     const bool dynamic = !partials && (h->opt_sched == 1 || (h->opt_sched < 0 && units * v.cg > h->grid));
     kp.tile_ctr = dynamic ? reinterpret_cast<int32_t *>(h->d_status) + 1 : nullptr;
 
@@ -722,6 +812,7 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
         tp.total_tiles = int32_t(tail_tiles);
         tp.band = 16;
         tp.tile_ctr = nullptr;
+        tp.tile_list = nullptr;
         tp.half_tiles = 0;
         tp.test_stall = 0;
         h->tail.fn = tv.fn[op][q.dtype];
@@ -744,9 +835,10 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     if (sk_tiles > 0)
         std::snprintf(form, sizeof(form), "split=1 stream_k=%lld tiles(<=%d pieces)", (long long)sk_tiles, ch.splits);
     else
-        std::snprintf(form, sizeof(form), "split=%d%s%s%s", ch.splits,
+        std::snprintf(form, sizeof(form), "split=%d%s%s%s%s%s", ch.splits,
                       split_tiles > 0 && split_tiles < tiles ? "(last wave)" : "", dynamic ? " dynamic" : "",
-                      half_tiles ? " half-tiles" : "");
+                      half_tiles ? " half-tiles" : "", planned ? " interleaved" : "",
+                      mn_chunks == 3 ? " chunk-boxes" : mn_chunks == 1 ? " chunk-boxes(dy)" : mn_chunks == 2 ? " chunk-boxes(x)" : "");
     char tail_form[96] = "";
     if (h->tail.active)
         std::snprintf(tail_form, sizeof(tail_form), " +tail gg_sm100 tile=128x%d cta_group=1 tiles=%lld grid=%d", bn,

@@ -93,6 +93,8 @@ enum : int { kOpForward = 0, kOpDgrad = 1, kOpWgrad = 2 };
 struct KernelParams {
     const int32_t *tile_off;  // [G+1] first tile of each group (cluster tiles)
     const int32_t *row_off;   // [G+1] first row (token) of each group in x / dy / out / dx
+    const int32_t *tile_list; // null: tiles in group order (tile_off, raster bands); else [total_tiles]
+                              // pairs (group, mt << 16 | nt): a tile order planned on the host
     const int32_t *row_cnt;   // null: group g has row_off[g+1] - row_off[g] rows; else [G] the rows this
                               // launch covers from row_off[g] (a split launch: the pair kernel takes each
                               // group's whole 256-row tiles, a one-CTA launch the remainders)
@@ -123,6 +125,9 @@ struct KernelParams {
                           // MMA wait on it runs out and the status word reports it
     int32_t half_tiles;   // 1: a group's last m-tile with at most 128 rows runs half height (pair
                           // variant, forward / dgrad, whole tiles; needs bn % 32 == 0)
+    int32_t mn_chunks;    // wgrad: bit 0 = the A maps (dy) and bit 1 = the B maps (x) are 3-D views
+                          // (64 columns, rows, 64-column chunks) whose one box covers all the 64-column
+                          // chunks a CTA loads per atom (else one 2-D box per chunk)
     int32_t *tile_ctr;    // non-null: dynamic tile dispatch (whole tiles only: splits <= 1, no
                           // stream-K). Cluster c takes tile c first, then tile C + atomicAdd(tile_ctr, 1)
                           // until past the last tile; 0 between launches (the last fetch resets it)
@@ -231,15 +236,55 @@ __host__ __device__ __forceinline__ int32_t ld_table(const int32_t *q) {
 #endif
 }
 
+// The group a role last decoded, with its table entries. A cluster's tile indices only grow
+// (static schedule, split units and dynamic dispatch alike), and consecutive tiles mostly belong to
+// one group, so decode_tile reads the tables only when a tile lies past the cached group: the
+// dependent global loads would otherwise stall each role for several hundred cycles per tile.
+struct GroupCursor {
+    int g = 0;         // group of the cached entries (the search starts here)
+    int t_begin = 0;   // tile_off[g]
+    int t_end = -1;    // tile_off[g + 1]; -1 = nothing cached
+    int r0 = 0;        // row_off[g]
+    int m = 0;         // rows of group g
+};
+
 template <int kClusterM, int kOp>
-__host__ __device__ __forceinline__ TileCoord decode_tile(const KernelParams &p, int t, int &cursor) {
-    while (ld_table(&p.tile_off[cursor + 1]) <= t)
-        ++cursor;
+__host__ __device__ __forceinline__ TileCoord decode_tile(const KernelParams &p, int t, GroupCursor &gc) {
     TileCoord tc;
-    tc.g = cursor;
-    const int local = t - ld_table(&p.tile_off[tc.g]);
-    const int r0 = ld_table(&p.row_off[tc.g]);
-    const int m = p.row_cnt ? ld_table(&p.row_cnt[tc.g]) : ld_table(&p.row_off[tc.g + 1]) - r0;
+    if (p.tile_list) {
+        // a planned order: the tile's coordinates come from the list (the cursor is not used)
+        tc.g = ld_table(&p.tile_list[2 * int64_t(t)]);
+        const int mn = ld_table(&p.tile_list[2 * int64_t(t) + 1]);
+        tc.mt = mn >> 16;
+        tc.nt = mn & 0xffff;
+        const int r0 = ld_table(&p.row_off[tc.g]);
+        const int m = p.row_cnt ? ld_table(&p.row_cnt[tc.g]) : ld_table(&p.row_off[tc.g + 1]) - r0;
+        if constexpr (kOp == kOpWgrad) {
+            tc.rows = p.tile_rows;
+            tc.out_row0 = tc.g * p.tile_rows;
+            tc.red_atoms = (m + kBK - 1) / kBK;
+        } else {
+            tc.rows = m;
+            tc.out_row0 = r0;
+            tc.red_atoms = p.num_kb;
+        }
+        tc.half = is_half_tile<kClusterM, kOp>(p.half_tiles, tc.rows, tc.mt);
+        return tc;
+    }
+    if (t >= gc.t_end || t < gc.t_begin) {
+        int g = t < gc.t_begin ? 0 : gc.g;
+        while (ld_table(&p.tile_off[g + 1]) <= t)
+            ++g;
+        gc.g = g;
+        gc.t_begin = ld_table(&p.tile_off[g]);
+        gc.t_end = ld_table(&p.tile_off[g + 1]);
+        gc.r0 = ld_table(&p.row_off[g]);
+        gc.m = p.row_cnt ? ld_table(&p.row_cnt[g]) : ld_table(&p.row_off[g + 1]) - gc.r0;
+    }
+    tc.g = gc.g;
+    const int local = t - gc.t_begin;
+    const int r0 = gc.r0;
+    const int m = gc.m;
     if constexpr (kOp == kOpWgrad) {
         tc.rows = p.tile_rows;
         tc.out_row0 = tc.g * p.tile_rows;
@@ -266,6 +311,17 @@ __host__ __device__ __forceinline__ TileCoord decode_tile(const KernelParams &p,
         tc.nt = b * p.band + (r - tc.mt * cols);
     }
     tc.half = is_half_tile<kClusterM, kOp>(p.half_tiles, tc.rows, tc.mt);
+    return tc;
+}
+
+// The same with a bare group cursor (host callers: the tile-order planner and the CPU tests).
+template <int kClusterM, int kOp>
+__host__ __device__ __forceinline__ TileCoord decode_tile(const KernelParams &p, int t, int &cursor) {
+    GroupCursor gc;
+    gc.g = cursor;
+    gc.t_begin = 0;  // nothing cached; the search starts at the cursor (t only grows)
+    const TileCoord tc = decode_tile<kClusterM, kOp>(p, t, gc);
+    cursor = gc.g;
     return tc;
 }
 
@@ -553,7 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // right after the dependency wait (decoding after it would wait on dependent global loads).
     // (Unit 0 is tile cluster_id with dynamic dispatch too: that needs whole tiles.)
     TileCoord first_tc{};
-    int first_cursor = 0;
+    GroupCursor first_cursor;
     if (warp <= 1 && units.n > 0)  // the producer, and the MMA warp (tile height, wgrad reduction)
         first_tc = decode_tile<C::kClusterM, kOp>(p, unit_at(p, units, cluster_id, num_clusters, 0).t, first_cursor);
     ptx::griddep_wait();
@@ -575,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         {
             const uint32_t issue = ptx::elect_one_sync();
             const uint32_t full_leader0 = kCG == 2 ? ptx::mapa(full_bar(0), 0) : full_bar(0);
-            int cursor = 0;
+            GroupCursor cursor;
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
@@ -684,14 +740,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const uint32_t ad = a_dst + a * C::kAAtomBytes;
                             const uint32_t bd = b_dst + a * b_atom_bytes;
                             if constexpr (kAMn) {
-                                // wgrad A = dy^T: two 64-column boxes of the group's dy rows
-                                load_2d<kCG>(ad, map_a, fb, a_row, k0, issue);
-                                load_2d<kCG>(ad + kMnBoxBytes, map_a, fb, a_row + 64, k0, issue);
+                                // wgrad A = dy^T: the CTA's two 64-column chunks of the group's dy
+                                // rows, one box of the 3-D chunk view or two 2-D boxes
+                                if (p.mn_chunks & 1) {
+                                    load_3d<kCG>(ad, map_a, fb, 0, k0, a_row / 64, issue);
+                                } else {
+                                    load_2d<kCG>(ad, map_a, fb, a_row, k0, issue);
+                                    load_2d<kCG>(ad + kMnBoxBytes, map_a, fb, a_row + 64, k0, issue);
+                                }
                             } else {
                                 load_2d<kCG>(ad, half ? static_cast<const void *>(&tmap_a_half) : map_a, fb, k0, a_row, issue);
                             }
                             if constexpr (kOp == kOpForward) {
                                 load_3d<kCG>(bd, map_b, fb, k0, b_row, tc.g, issue);
+                            } else if (kOp == kOpWgrad && (p.mn_chunks & 2)) {
+                                // x rows (tokens) k0.. of the group, all b_rows / 64 chunks at once
+                                load_3d<kCG>(bd, map_b, fb, 0, k0, b_row / 64, issue);
                             } else {
                                 for (int j = 0; j < b_rows / 64; ++j) {
                                     if constexpr (kOp == kOpDgrad)  // w[g] rows k0.., columns b_row + 64j..
@@ -728,7 +792,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            int cursor = 0;
+            GroupCursor cursor;
             for (int i = 0; ok; ++i, ++tl) {
                 Unit un;
                 if (dyn) {
@@ -834,7 +898,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t out_stage = smem_base + C::kOutOffset + uint32_t(q) * 2u * C::kStageOutBytes;
         const uint64_t store_policy = ptx::l2_policy_evict_first();  // out is never re-read here
         int out_buf = 0;
-        int cursor = 0;
+        GroupCursor cursor;
         uint32_t tl = 0;
         for (int i = 0;; ++i, ++tl) {
             Unit un;
@@ -1106,7 +1170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) {
                 if constexpr (kCG == 2)
-                    ptx::mbar_arrive_cluster(tempty_leader0 + 8u * acc);
+                    ptx::mbar_arrive_cluster_cta(tempty_leader0 + 8u * acc);
                 else
                     ptx::mbar_arrive(tempty_bar(acc));
             }

@@ -97,6 +97,15 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
                  : "memory");
 }
 
+// The same arrive with CTA-scope release, for a signal that publishes no memory the waiter reads:
+// an accumulator's release to the MMA warp after tcgen05.wait::ld (the tcgen05 fences around the
+// barrier order the TMEM accesses). A cluster-scope release would first wait until this warp's
+// earlier global stores are performed at cluster scope, which costs the epilogue of a short tile
+// about as much as its own stores.
+__device__ __forceinline__ void mbar_arrive_cluster_cta(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
 // Test (and briefly wait for) completion of the phase with the given parity.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;

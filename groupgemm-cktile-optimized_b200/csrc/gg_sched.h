@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <vector>
 
 #include "gg_b200.h"
 #include "gg_kernel.cuh"
@@ -192,6 +193,45 @@ inline Choice choose_tiling(const TileShape *shapes, int nshapes, const gg_probl
         }
     }
     return best;
+}
+
+// Planned tile order for launches whose tiles cost very different amounts (wgrad under skewed
+// routing: an expert with few tokens has a short reduction, so its tiles are bound by their stores
+// -- a whole tile of output each -- while a large expert's tiles are bound by the tensor pipe). In
+// group order the two kinds run as separate phases, first one resource idle, then the other.
+// `natural` holds the tiles in group order as pairs (group, mt << 16 | nt); `cost[g]` estimates
+// a tile's cycles and `store_bound[g]` its kind. The two kinds are merged so that each has
+// dispatched the same fraction of its total estimated work at every point (ties to the
+// tensor-bound kind); within a kind the group order is kept. With dynamic dispatch, each cluster
+// then takes the next tile of the merged list as it finishes one, so stores and MMAs overlap.
+inline void interleave_tiles(const std::vector<int32_t> &natural, const std::vector<double> &cost,
+                             const std::vector<char> &store_bound, std::vector<int32_t> &out) {
+    const size_t n = natural.size() / 2;
+    double total[2] = {0, 0};
+    std::vector<size_t> idx[2];
+    for (size_t i = 0; i < n; ++i) {
+        const int g = natural[2 * i];
+        const int k = store_bound[size_t(g)] ? 1 : 0;
+        idx[k].push_back(i);
+        total[k] += cost[size_t(g)];
+    }
+    out.clear();
+    out.reserve(natural.size());
+    size_t pos[2] = {0, 0};
+    double done[2] = {0, 0};
+    while (pos[0] < idx[0].size() || pos[1] < idx[1].size()) {
+        int k;
+        if (pos[0] >= idx[0].size())
+            k = 1;
+        else if (pos[1] >= idx[1].size())
+            k = 0;
+        else
+            k = done[0] / total[0] <= done[1] / total[1] ? 0 : 1;
+        const size_t i = idx[k][pos[k]++];
+        out.push_back(natural[2 * i]);
+        out.push_back(natural[2 * i + 1]);
+        done[k] += cost[size_t(natural[2 * i])];
+    }
 }
 
 }  // namespace gg

@@ -9,13 +9,15 @@
 //   * a tile cut into pieces has workspace: n <= splits (the stride) and the tile is a split tile;
 //   * stream-K: every piece but piece 0 is the first unit of its cluster, so the fixed summer
 //     (piece 0) only ever waits for units that wait on nothing themselves (no circular wait).
-// The dynamic tile dispatch is played out in random fetch orders (check_dynamic), and the
-// half-height tile flag is checked on every decoded tile.
+// The dynamic tile dispatch is played out in random fetch orders (check_dynamic), the
+// half-height tile flag is checked on every decoded tile, and the planned (interleaved) tile
+// order is checked (check_interleave).
 // Then decode_tile, for random group sizes (empty groups included), widths, bands and both raster
 // orders: tile indices map onto every (group, m-tile, n-tile) exactly once.
 // Prints "ok <launches> <units> <tables>" and exits 0, or prints the first violation and exits 1.
 // With `choose B,M,N,K ...` it prints the cost model's automatic choice for each problem instead.
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <string>
@@ -137,10 +139,17 @@ bool check_decode(const std::vector<int64_t> &group_m, int tiles_n, int band, in
     p.tile_rows = tile_rows;
     std::vector<char> hit(size_t(tiles), 0);
     int cursor = 0;
+    gg::GroupCursor gcur;
     for (int64_t t = 0; t < tiles; ++t) {
         const gg::TileCoord tc = gg::decode_tile<kCM, kOp>(p, int(t), cursor);
         int fresh = 0;
         const gg::TileCoord tf = gg::decode_tile<kCM, kOp>(p, int(t), fresh);
+        const gg::TileCoord tg = gg::decode_tile<kCM, kOp>(p, int(t), gcur);  // the kernel's cached form
+        if (tg.g != tc.g || tg.mt != tc.mt || tg.nt != tc.nt || tg.rows != tc.rows || tg.out_row0 != tc.out_row0 ||
+            tg.red_atoms != tc.red_atoms || tg.half != tc.half) {
+            std::printf("FAIL decode_tile with a group cache: tile %lld\n", (long long)t);
+            return false;
+        }
         const int g = tc.g;
         const int64_t m_rows = kOp == gg::kOpWgrad ? tile_rows : group_m[size_t(g)];
         const int tiles_m = int((m_rows + kCM - 1) / kCM);
@@ -166,6 +175,21 @@ bool check_decode(const std::vector<int64_t> &group_m, int tiles_n, int band, in
         if (hit.at(static_cast<std::size_t>(idx))++) {
             std::printf("FAIL decode_tile: tile (%d, %d, %d) decoded twice\n", g, tc.mt, tc.nt);
             return false;
+        }
+    }
+    // a cluster's strided walk (tiles c, c + C, ...) with one cached cursor, as each role runs it
+    for (const int C : {3, 74, 148}) {
+        for (int c = 0; c < C && c < tiles; c += 7) {
+            gg::GroupCursor gc;
+            for (int64_t t = c; t < tiles; t += C) {
+                int fresh = 0;
+                const gg::TileCoord tf = gg::decode_tile<kCM, kOp>(p, int(t), fresh);
+                const gg::TileCoord tg = gg::decode_tile<kCM, kOp>(p, int(t), gc);
+                if (tg.g != tf.g || tg.mt != tf.mt || tg.nt != tf.nt || tg.rows != tf.rows || tg.red_atoms != tf.red_atoms) {
+                    std::printf("FAIL decode_tile with a group cache, stride %d: tile %lld\n", C, (long long)t);
+                    return false;
+                }
+            }
         }
     }
     return true;
@@ -209,6 +233,99 @@ bool check_dynamic(Rng &rng, int tiles, int C) {
         if (!all || ctr != 0 || fetches != tiles) {
             std::printf("FAIL dynamic dispatch: tiles %d clusters %d covered %d counter %d fetches %d\n", tiles, C,
                         int(all), ctr, fetches);
+            return false;
+        }
+    }
+    return true;
+}
+
+// Planned tile order (interleave_tiles, as gg_prepare builds it for wgrad): for random group
+// tables, the merged list is a permutation of the group-order tiles, keeps the group order within
+// each kind, keeps the two kinds' dispatched work fractions within one tile's share of each other,
+// and decode_tile over the list returns the listed tiles.
+bool check_interleave(Rng &rng) {
+    const int G = rng.range(1, 40);
+    std::vector<int64_t> gm(static_cast<size_t>(G));
+    for (auto &m : gm)
+        m = rng.range(1, 5) == 1 ? 0 : (rng.range(1, 3) == 1 ? rng.range(1, 120) : rng.range(1, 30000));
+    const int tile_rows = 256 * rng.range(1, 6), tiles_n = rng.range(1, 12);
+    std::vector<int32_t> tile_off(static_cast<size_t>(G) + 1), row_off(static_cast<size_t>(G) + 1);
+    int64_t tiles = 0, rows = 0;
+    for (int g = 0; g < G; ++g) {
+        tile_off[size_t(g)] = int32_t(tiles);
+        row_off[size_t(g)] = int32_t(rows);
+        tiles += (tile_rows + 255) / 256 * tiles_n;
+        rows += gm[size_t(g)];
+    }
+    tile_off[size_t(G)] = int32_t(tiles);
+    row_off[size_t(G)] = int32_t(rows);
+    gg::KernelParams p{};
+    p.tile_off = tile_off.data();
+    p.row_off = row_off.data();
+    p.tiles_n = tiles_n;
+    p.band = rng.range(1, 9);
+    p.tile_rows = tile_rows;
+    std::vector<int32_t> natural(2 * size_t(tiles)), order;
+    int cursor = 0;
+    for (int64_t t = 0; t < tiles; ++t) {
+        const gg::TileCoord tc = gg::decode_tile<256, gg::kOpWgrad>(p, int(t), cursor);
+        natural[2 * size_t(t)] = tc.g;
+        natural[2 * size_t(t) + 1] = (tc.mt << 16) | tc.nt;
+    }
+    std::vector<double> cost(static_cast<size_t>(G));
+    std::vector<char> sb(static_cast<size_t>(G));
+    double total[2] = {0, 0}, most = 0;
+    for (int g = 0; g < G; ++g) {
+        const double mma = double((gm[size_t(g)] + 63) / 64) * 4.0 * 128.0, epi = 2816.0;
+        cost[size_t(g)] = std::max(mma, epi);
+        sb[size_t(g)] = mma < epi;
+        total[sb[size_t(g)]] += cost[size_t(g)] * tiles_n * ((tile_rows + 255) / 256);
+    }
+    gg::interleave_tiles(natural, cost, sb, order);
+    if (order.size() != natural.size()) {
+        std::printf("FAIL interleave: size\n");
+        return false;
+    }
+    std::vector<std::pair<int32_t, int32_t>> a, b;
+    for (size_t i = 0; i < natural.size(); i += 2) {
+        a.push_back({natural[i], natural[i + 1]});
+        b.push_back({order[i], order[i + 1]});
+    }
+    std::vector<std::pair<int32_t, int32_t>> sa = a, sb2 = b;
+    std::sort(sa.begin(), sa.end());
+    std::sort(sb2.begin(), sb2.end());
+    if (sa != sb2) {
+        std::printf("FAIL interleave: not a permutation\n");
+        return false;
+    }
+    // order within each kind, and the balance of dispatched work
+    std::vector<std::pair<int32_t, int32_t>> kind_nat[2], kind_ord[2];
+    for (auto &x : a)
+        kind_nat[sb[size_t(x.first)]].push_back(x);
+    double done[2] = {0, 0};
+    for (auto &x : b) {
+        const int k = sb[size_t(x.first)];
+        kind_ord[k].push_back(x);
+        done[k] += cost[size_t(x.first)];
+        most = std::max(most, cost[size_t(x.first)]);
+        if (total[0] > 0 && total[1] > 0 && done[0] < total[0] && done[1] < total[1] &&
+            std::fabs(done[0] / total[0] - done[1] / total[1]) > most / std::min(total[0], total[1]) + 1e-9) {
+            std::printf("FAIL interleave: kinds out of balance\n");
+            return false;
+        }
+    }
+    if (kind_nat[0] != kind_ord[0] || kind_nat[1] != kind_ord[1]) {
+        std::printf("FAIL interleave: order within a kind changed\n");
+        return false;
+    }
+    // decode_tile over the planned list returns the listed tiles
+    p.tile_list = order.data();
+    for (int64_t t = 0; t < tiles; ++t) {
+        int unused = 0;
+        const gg::TileCoord tc = gg::decode_tile<256, gg::kOpWgrad>(p, int(t), unused);
+        if (tc.g != order[2 * size_t(t)] || ((tc.mt << 16) | tc.nt) != order[2 * size_t(t) + 1] ||
+            tc.rows != tile_rows || tc.red_atoms != int((gm[size_t(tc.g)] + 63) / 64)) {
+            std::printf("FAIL interleave: decode of the list\n");
             return false;
         }
     }
@@ -278,6 +395,9 @@ int main(int argc, char **argv) {
         if (!check_dynamic(rng, tiles, C))
             return 1;
     }
+    for (int n = 0; n < launches / 100; ++n)
+        if (!check_interleave(rng))
+            return 1;
     std::printf("ok %d %lld %d\n", done, units, decoded);
     return 0;
 }

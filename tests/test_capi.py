@@ -77,11 +77,13 @@ def test_set_option(gg):
                      ("pdl", 0), ("pdl", 1), ("store", -1), ("store", 0), ("store", 1), ("stream_k", -1),
                      ("stream_k", 0), ("stream_k", 1), ("stream_k", 2), ("bn", 240), ("bn", 16), ("bn", 0),
                      ("sched", -1), ("sched", 0), ("sched", 1), ("half_tiles", -1), ("half_tiles", 0), ("half_tiles", 1),
-                     ("tail_launch", -1), ("tail_launch", 0), ("tail_launch", 1), ("test_bounds", 0), ("test_bounds", 1)):
+                     ("tail_launch", -1), ("tail_launch", 0), ("tail_launch", 1), ("test_bounds", 0), ("test_bounds", 1),
+                     ("tile_order", -1), ("tile_order", 0), ("tile_order", 1), ("tma_chunks", 0), ("tma_chunks", 1)):
         b.set_option(key, val)
     for key, val in (("variant", 7), ("band", -1), ("timeout_ms", 0), ("test_stall", 2), ("bn", 100), ("bn", 288), ("split", 9),
                      ("split_tail", 2), ("raster", 2), ("pdl", 3), ("store", 2), ("bogus", 1), ("bn", 24), ("bn", 8),
-                     ("stream_k", 3), ("stream_k", -2), ("sched", 2), ("sched", -2), ("half_tiles", 2), ("tail_launch", 2), ("test_bounds", 2)):
+                     ("stream_k", 3), ("stream_k", -2), ("sched", 2), ("sched", -2), ("half_tiles", 2), ("tail_launch", 2), ("test_bounds", 2),
+                     ("tile_order", 2), ("tile_order", -2), ("tma_chunks", 2), ("tma_chunks", -1)):
         with pytest.raises(gg.GGError):
             b.set_option(key, val)
 

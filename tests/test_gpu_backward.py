@@ -31,7 +31,7 @@ def upload(torch, bits):
     return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).cuda()
 
 
-def run_grad(gg, op, group_m, n, k, dtype, dy, x, w, variant=-1, bn=0, split=0, band=0, runs=1):
+def run_grad(gg, op, group_m, n, k, dtype, dy, x, w, variant=-1, bn=0, split=0, band=0, runs=1, opts=None):
     """Prepare and run one backward op; returns (output bits, detail)."""
     torch = _torch()
     total = int(sum(group_m))
@@ -46,6 +46,8 @@ def run_grad(gg, op, group_m, n, k, dtype, dy, x, w, variant=-1, bn=0, split=0, 
         b.set_option("split", split)
     if band:
         b.set_option("band", band)
+    for key, val in (opts or {}).items():
+        b.set_option(key, val)
     s = torch.cuda.current_stream().cuda_stream
     ptr = lambda t: t.data_ptr() if t is not None and t.numel() else 0  # noqa: E731
     if op == gg.OP_DGRAD:
@@ -118,6 +120,35 @@ def test_tile_widths(gg, orc, name, variant, bn):
 def test_dgrad_split_k(gg, orc, variant, split):
     # split-K over N (the dgrad reduction); two launches in a row reuse the arrival counters
     grad_case(gg, orc, gg.OP_DGRAD, [300, 0, 17, 513], 1000, 256, 0, (variant,), split=split, runs=2)
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+@pytest.mark.parametrize("group_m,n,k,variant,bn,mode", [
+    ([300, 0, 65, 1000, 7], 512, 384, 0, 256, 3),     # both operands in chunk boxes, pair tile
+    ([300, 0, 65, 1000, 7], 320, 448, 0, 128, 3),     # N tail inside a 256-row tile, one chunk of x per CTA
+    ([130, 64, 1], 448, 200, 1, 192, 1),              # K % 64 != 0: dy in chunk boxes, x in 2-D boxes
+    ([130, 64, 1], 200, 256, 1, 256, 2),              # N % 64 != 0: x in chunk boxes (4 per box)
+    ([500, 33], 256, 320, 2, 128, 3),                 # one-CTA 128 x 128 tile
+    ([2000, 129, 0, 64], 768, 1024, -1, 0, 3),        # automatic tiling
+])
+def test_wgrad_chunk_boxes_match_2d_boxes(gg, orc, dtype, group_m, n, k, variant, bn, mode):
+    """wgrad's MN-major operands loaded through the 3-D chunk view (one box per operand and atom)
+    give the same bits as one 2-D box per 64-column chunk, and pass the oracle's full compare;
+    shapes whose N (dy) or K (x) is not a multiple of 64 keep the 2-D boxes for that operand."""
+    torch = _torch()
+    dy, x, w = orc.make_grad_inputs(group_m, n, k, dtype)
+    ref = orc.grouped_wgrad_f32(dy, x, group_m, dtype).reshape(-1, k)
+    dyd, xd, wd = upload(torch, dy), upload(torch, x), upload(torch, w)
+    got = {}
+    for chunks in (0, 1):
+        res, detail = run_grad(gg, gg.OP_WGRAD, group_m, n, k, dtype, dyd, xd, wd, variant=variant, bn=bn, runs=2,
+                               opts={"tma_chunks": chunks})
+        tag = {3: "chunk-boxes ", 1: "chunk-boxes(dy)", 2: "chunk-boxes(x)"}[mode]
+        assert (tag in detail + " ") == (chunks == 1), detail
+        bad, mx, first = orc.check16(res, ref, dtype)
+        assert bad == 0, f"tma_chunks={chunks} ({detail}): {bad} mismatches, first at {divmod(first, k)}, max abs {mx}"
+        got[chunks] = res
+    assert np.array_equal(got[0], got[1])
 
 
 def test_wgrad_every_expert_empty_writes_zeros(gg, orc):

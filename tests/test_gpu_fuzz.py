@@ -54,6 +54,10 @@ def draw_case(rng):
         opts["half_tiles"] = int(rng.integers(0, 2))
     if rng.random() < 0.5:
         opts["tail_launch"] = int(rng.integers(0, 2))  # otherwise automatic (skewed remainders)
+    if rng.random() < 0.4:
+        opts["tile_order"] = int(rng.integers(0, 2))  # wgrad: group order or interleaved (else automatic)
+    if rng.random() < 0.3:
+        opts["tma_chunks"] = 0  # wgrad: one 2-D box per 64-column chunk instead of the 3-D chunk view
     return group_m, n, k, op, dtype, opts
 
 

@@ -729,3 +729,61 @@ def test_split_launch_for_skewed_routing(gg, orc, dtype, op, group_m):
             bad, _, _ = orc.check16(out.cpu().numpy().view(np.uint16)[:rows * cols].reshape(rows, cols), ref, dtype)
             assert bad == 0, (b.detail(), "graph replay")
         b.release()
+
+
+@pytest.mark.parametrize("sched", [0, 1])
+@pytest.mark.parametrize("dtype", [0, 1])
+@pytest.mark.parametrize("variant,bn,max_ctas", [(-1, 0, 0), (0, 256, 10), (1, 192, 0), (2, 128, 7)])
+def test_wgrad_interleaved_tile_order(gg, orc, sched, dtype, variant, bn, max_ctas):
+    """wgrad under skewed routing: groups with a few rows (a short reduction, bound by their output
+    stores), empty groups and groups with thousands of rows. The host-planned interleaved tile
+    order ("tile_order" 1, and the automatic choice for this mix) runs every tile once: three
+    launches in a row and a graph replay give the bits of the group-order launch and pass the
+    oracle's full compare."""
+    torch = _torch()
+    group_m, n, k = [2100, 5, 0, 64, 1500, 17, 130, 700, 1, 40, 300], 512, 384
+    s = torch.cuda.current_stream().cuda_stream
+    dy, x, _ = orc.make_grad_inputs(group_m, n, k, dtype)
+    up = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda()  # noqa: E731
+    dyd, xd = up(dy), up(x)
+    ref = orc.grouped_wgrad_f32(dy, x, group_m, dtype).reshape(-1, k)
+    rows, cols = len(group_m) * n, k
+    results = {}
+    for order in (0, 1, -1):
+        out = torch.full((rows * cols + GUARD,), CANARY, dtype=torch.int16, device="cuda")
+        b = gg.B200Backend()
+        b.set_option("tile_order", order)
+        b.set_option("sched", sched)
+        for key, val in {"variant": variant, "bn": bn, "max_ctas": max_ctas}.items():
+            if key == "variant" or val:
+                b.set_option(key, val)
+        why = b.prepare_grad(gg.OP_WGRAD, dtype, group_m, n, k, dy_ptr=dyd.data_ptr(), x_ptr=xd.data_ptr(),
+                             dw_ptr=out.data_ptr(), stream=s)
+        assert why == "", why
+        assert ("interleaved" in b.detail()) == (order != 0), b.detail()
+        runs = []
+        for _ in range(3):
+            out[:rows * cols].fill_(0)
+            b.run(s)
+            assert b.device_status(s) == 0, b.detail()
+            res = out.cpu().numpy().view(np.uint16)
+            assert np.all(res[rows * cols:] == CANARY), (b.detail(), "store past the end of dw")
+            runs.append(res[:rows * cols].reshape(rows, cols).copy())
+        graph_stream = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=graph_stream):
+            for _ in range(2):
+                b.run(torch.cuda.current_stream().cuda_stream)
+        out[:rows * cols].fill_(0)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        assert b.device_status(s) == 0, b.detail()
+        runs.append(out[:rows * cols].cpu().numpy().view(np.uint16).reshape(rows, cols).copy())
+        del g
+        assert all(np.array_equal(runs[0], r) for r in runs[1:]), b.detail()
+        bad, mx, first = orc.check16(runs[0], ref, dtype)
+        assert bad == 0, (b.detail(), bad, mx, first)
+        results[order] = runs[0]
+        b.release()
+    assert np.array_equal(results[0], results[1]) and np.array_equal(results[0], results[-1])
