@@ -735,21 +735,37 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     kp.ws_float4s = partials ? int64_t(h->ws_cap / 16) : 0;
     kp.ctr_entries = partials ? int32_t(h->counters_cap / sizeof(int32_t)) : 0;
     kp.timeout_ns = uint64_t(h->opt_timeout_ms) * 1000000ull;
-    // Planned tile order (wgrad under skewed routing): an expert with few tokens has a short
-    // reduction, so its tiles are bound by their stores (a whole tile of output each), a large
-    // expert's by the tensor pipe. In group order the two kinds run as separate phases; the
-    // interleaved order (gg::interleave_tiles) with dynamic dispatch lets them overlap. Estimates
-    // per tile: bn/2 cycles per MMA (the tensor rate), ~11 bn cycles for the epilogue's stores.
+    // Planned tile order (skewed routing): tiles of two kinds, bound by different resources, run
+    // as separate phases in group order; the interleaved order (gg::interleave_tiles) with dynamic
+    // dispatch lets them overlap.
+    //   wgrad: an expert with few tokens has a short reduction, so its tiles are bound by their
+    //     stores (a whole tile of output each), a large expert's by the tensor pipe. Estimates per
+    //     tile: bn/2 cycles per MMA (the tensor rate), ~11 bn cycles for the epilogue's stores.
+    //   forward / dgrad (one launch, no split launch): a tile streams its weight panel (bn/kCG rows
+    //     of the reduction per CTA) from DRAM once per group, shared by the group's m-tiles; an
+    //     expert with few tokens has few m-tiles to share it, so its tiles are bound by DRAM
+    //     (~40 B/cycle per SM, its share of HBM), a large expert's by the tensor pipe (bn/2 cycles
+    //     per MMA, half that for a half-height tile).
     bool planned = false;
-    if (op == gg::kOpWgrad && !partials && h->opt_order != 0 && tiles > 0) {
+    const bool plan_ok = op == gg::kOpWgrad || !tail;
+    if (plan_ok && !partials && h->opt_order != 0 && tiles > 0) {
         std::vector<double> cost(size_t(G), 0.0);
         std::vector<char> store_bound(size_t(G), 0);
         double work[2] = {0, 0};
         const double epi = 11.0 * bn;
         for (int g = 0; g < G; ++g) {
-            const double mma = double((q.group_m[g] + gg::kBK - 1) / gg::kBK) * 4.0 * 0.5 * bn;
-            cost[size_t(g)] = std::max(mma, epi);
-            store_bound[size_t(g)] = mma < epi ? 1 : 0;
+            double mma, other;
+            if (op == gg::kOpWgrad) {
+                mma = double((q.group_m[g] + gg::kBK - 1) / gg::kBK) * 4.0 * 0.5 * bn;
+                other = epi;
+            } else {
+                const int64_t mtiles = std::max<int64_t>(1, (q.group_m[g] + v.cluster_m - 1) / v.cluster_m);
+                const bool half_only = half_tiles && mtiles == 1 && q.group_m[g] <= v.cluster_m / 2;
+                mma = double(kp.num_kb) * 4.0 * 0.5 * bn * (half_only ? 0.5 : 1.0);
+                other = double(bn / v.cg) * double(kp.k) * 2.0 / 40.0 / double(mtiles);
+            }
+            cost[size_t(g)] = std::max(mma, other);
+            store_bound[size_t(g)] = mma < other ? 1 : 0;
             work[store_bound[size_t(g)]] += cost[size_t(g)] * double(meta[size_t(g) + 1] - meta[size_t(g)]);
         }
         const double all = work[0] + work[1];
@@ -764,8 +780,13 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
             std::vector<int32_t> natural(2 * size_t(tiles)), order;
             int cursor = 0;
             for (int64_t t = 0; t < tiles; ++t) {
-                const gg::TileCoord tc = v.cluster_m == 256 ? gg::decode_tile<256, gg::kOpWgrad>(hp, int(t), cursor)
-                                                            : gg::decode_tile<128, gg::kOpWgrad>(hp, int(t), cursor);
+                gg::TileCoord tc;
+                if (op == gg::kOpWgrad)
+                    tc = v.cluster_m == 256 ? gg::decode_tile<256, gg::kOpWgrad>(hp, int(t), cursor)
+                                            : gg::decode_tile<128, gg::kOpWgrad>(hp, int(t), cursor);
+                else
+                    tc = v.cluster_m == 256 ? gg::decode_tile<256, gg::kOpForward>(hp, int(t), cursor)
+                                            : gg::decode_tile<128, gg::kOpForward>(hp, int(t), cursor);
                 natural[2 * size_t(t)] = tc.g;
                 natural[2 * size_t(t) + 1] = (tc.mt << 16) | tc.nt;
             }

@@ -169,15 +169,19 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
  *                256-row tile holds at most 128 rows runs that tile half height (an M = 128 pair
  *                MMA, 64 rows per CTA). Measured slower than the split launch and than padding on
  *                B200 (a half tile costs ~0.9 of a whole one), so it is off unless asked for
- *   "tile_order" wgrad only (no split-K): 0 group order (default), 1 interleaved, -1 interleaved
- *                when each kind below holds at least 5% of the launch's cost. With interleaving,
- *                gg_prepare plans the launch's tile order on the host: tiles of groups with a
- *                short reduction (few rows, bound by their output stores) and tiles of groups
- *                with a long one (bound by the tensor cores) are merged so that both kinds are
- *                dealt out at the same fraction of their total cost, and the list is copied to the
- *                handle's device memory; "sched" still picks static or dynamic dispatch over it.
- *                Measured slower than group order on B200 (skewed routing, 256 experts: 707
- *                static / 764 dynamic vs 815 TFLOPS), so it is off unless asked for
+ *   "tile_order" whole tiles (no split-K), and for forward / dgrad one launch (no split launch):
+ *                0 group order (default), 1 interleaved, -1 interleaved when each kind below holds
+ *                at least 5% of the launch's cost. With interleaving, gg_prepare plans the launch's
+ *                tile order on the host: tiles of two kinds are merged so that both are dealt out
+ *                at the same fraction of their total cost, and the list is copied to the handle's
+ *                device memory; "sched" still picks static or dynamic dispatch over it. The kinds:
+ *                wgrad, groups with a short reduction (few rows, bound by their output stores) and
+ *                groups with a long one (bound by the tensor cores); forward / dgrad, groups with
+ *                few m-tiles (bound by reading their weight panels from DRAM) and groups with many.
+ *                Measured on B200 under skewed routing (256 experts): wgrad slower than group order
+ *                (707 static / 764 dynamic vs 815 TFLOPS); forward with half tiles and dynamic
+ *                dispatch level with the split launch at the power cap (1034 vs 1059 TFLOPS), so
+ *                it is off unless asked for
  *   "pdl"        1 (default) = launch with programmatic stream serialisation, so the launch and
  *                on-chip set-up overlap the previous kernel in the stream; 0 = plain launch
  *   "max_ctas"   cap on the persistent grid (0 = one CTA per SM)

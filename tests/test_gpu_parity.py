@@ -787,3 +787,57 @@ def test_wgrad_interleaved_tile_order(gg, orc, sched, dtype, variant, bn, max_ct
         results[order] = runs[0]
         b.release()
     assert np.array_equal(results[0], results[1]) and np.array_equal(results[0], results[-1])
+
+
+@pytest.mark.parametrize("opts", [
+    {"variant": 0, "sched": 1, "half_tiles": 1},
+    {"variant": 0, "sched": 0, "half_tiles": 0, "max_ctas": 10},
+    {"variant": 1, "bn": 192, "sched": 1},
+    {"variant": 2, "bn": 128, "sched": 1, "max_ctas": 7},
+])
+@pytest.mark.parametrize("op", ["forward", "dgrad"])
+def test_forward_dgrad_interleaved_tile_order(gg, orc, opts, op):
+    """Forward and dgrad under skewed routing in one launch (no split launch): the host-planned
+    interleaved order ("tile_order" 1) deals the tiles of experts with few tokens (bound by
+    reading their weight panels) among those of large experts (bound by the tensor pipe). Every
+    tile runs once: three launches give the bits of the group-order launch and pass the oracle's
+    full compare."""
+    torch = _torch()
+    group_m, n, k = [2100, 5, 0, 64, 1500, 17, 130, 700, 1, 40, 300], 512, 384
+    s = torch.cuda.current_stream().cuda_stream
+    up = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda()  # noqa: E731
+    if op == "forward":
+        x, w = orc.make_inputs(group_m, n, k, 0)
+        ref, rows, cols = orc.grouped_gemm_f32(x, w, group_m, 0), sum(group_m), n
+        xd, wd = up(x), up(w)
+    else:
+        dy, x, w = orc.make_grad_inputs(group_m, n, k, 0)
+        ref, rows, cols = orc.grouped_dgrad_f32(dy, w, group_m, 0), sum(group_m), k
+        dyd, wd = up(dy), up(w)
+    results = {}
+    for order in (0, 1):
+        out = torch.full((rows * cols + GUARD,), CANARY, dtype=torch.int16, device="cuda")
+        b = gg.B200Backend()
+        for key, val in {**opts, "tile_order": order, "tail_launch": 0, "split": 1}.items():
+            b.set_option(key, val)
+        if op == "forward":
+            why = b.prepare(0, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s)
+        else:
+            why = b.prepare_grad(gg.OP_DGRAD, 0, group_m, n, k, dy_ptr=dyd.data_ptr(), w_ptr=wd.data_ptr(),
+                                 dx_ptr=out.data_ptr(), stream=s)
+        assert why == "", why
+        assert ("interleaved" in b.detail()) == (order == 1), b.detail()
+        runs = []
+        for _ in range(3):
+            out[:rows * cols].fill_(0)
+            b.run(s)
+            assert b.device_status(s) == 0, b.detail()
+            res = out.cpu().numpy().view(np.uint16)
+            assert np.all(res[rows * cols:] == CANARY), (b.detail(), "store past the end of out")
+            runs.append(res[:rows * cols].reshape(rows, cols).copy())
+        assert all(np.array_equal(runs[0], r) for r in runs[1:]), b.detail()
+        bad, mx, first = orc.check16(runs[0], ref, 0)
+        assert bad == 0, (b.detail(), bad, mx, first)
+        results[order] = runs[0]
+        b.release()
+    assert np.array_equal(results[0], results[1])
