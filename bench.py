@@ -312,14 +312,18 @@ def roofline(flops, alg_bytes, ms_launch, peaks, peak_src, captures, kernel_deta
                     "traffic_gbs": round(traffic / (ms_launch * 1e-3) / 1e9, 1) if traffic else None}}
 
 
-def run_backward(args, cfg):
-    """Device-timed backward grouped GEMM (dgrad or wgrad) on one GPU, beside a per-group cuBLAS
-    loop (torch.matmul) of the same op on the same tensors. One JSON line; not the driver's
-    headline (that is the forward op)."""
+def run_vs_loop(args, cfg):
+    """One grouped GEMM (forward, dgrad or wgrad) on one GPU beside a per-group cuBLAS loop
+    (torch.matmul, one stream) of the same op on the same tensors. The two arms alternate in
+    rounds of a few steps each, so both see the same clocks and power state (at the 1000 W cap the
+    clock moves by 30% within seconds); each arm's figure is its median round. One JSON line; not
+    the driver's headline (that is the forward op through the full bench line)."""
+    import statistics
+
     import torch
 
     gg = load_package()
-    op = gg.OP_DGRAD if args.op == "dgrad" else gg.OP_WGRAD
+    op = {"forward": gg.OP_FORWARD, "dgrad": gg.OP_DGRAD, "wgrad": gg.OP_WGRAD}[args.op]
     dtype = gg.DTYPES[cfg["dtype"]]
     tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
     torch.cuda.set_device(0)
@@ -329,14 +333,24 @@ def run_backward(args, cfg):
     group_m = group_sizes(cfg, g0, g1)
     rows = sum(group_m)
     gen = torch.Generator(device="cuda").manual_seed(1000)
-    dy = torch.randn(rows, n, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
-    if op == gg.OP_DGRAD:
-        b_op = torch.empty(ng, n, k, device="cuda", dtype=tdt)
+
+    def randn(*shape):
+        return torch.randn(*shape, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
+
+    def weights():
+        w = torch.empty(ng, n, k, device="cuda", dtype=tdt)
         for g in range(ng):
-            b_op[g] = torch.randn(n, k, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
+            w[g] = randn(n, k)
+        return w
+
+    if op == gg.OP_FORWARD:
+        a_op, b_op = randn(rows, k), weights()
+        out = torch.empty(rows, n, device="cuda", dtype=tdt)
+    elif op == gg.OP_DGRAD:
+        a_op, b_op = randn(rows, n), weights()
         out = torch.empty(rows, k, device="cuda", dtype=tdt)
     else:
-        b_op = torch.randn(rows, k, device="cuda", generator=gen, dtype=torch.float32).to(tdt)
+        a_op, b_op = randn(rows, n), randn(rows, k)
         out = torch.empty(ng, n, k, device="cuda", dtype=tdt)
     stream = torch.cuda.Stream()
     s = stream.cuda_stream
@@ -346,48 +360,75 @@ def run_backward(args, cfg):
     for kv in args.opt:
         key, _, val = kv.partition("=")
         be.set_option(key, int(val))
-    if op == gg.OP_DGRAD:
-        why = be.prepare_grad(op, dtype, group_m, n, k, dy_ptr=dy.data_ptr(), w_ptr=b_op.data_ptr(),
+    if op == gg.OP_FORWARD:
+        why = be.prepare(dtype, group_m, n, k, a_op.data_ptr(), b_op.data_ptr(), out.data_ptr(), s)
+    elif op == gg.OP_DGRAD:
+        why = be.prepare_grad(op, dtype, group_m, n, k, dy_ptr=a_op.data_ptr(), w_ptr=b_op.data_ptr(),
                               dx_ptr=out.data_ptr(), stream=s)
     else:
-        why = be.prepare_grad(op, dtype, group_m, n, k, dy_ptr=dy.data_ptr(), x_ptr=b_op.data_ptr(),
+        why = be.prepare_grad(op, dtype, group_m, n, k, dy_ptr=a_op.data_ptr(), x_ptr=b_op.data_ptr(),
                               dw_ptr=out.data_ptr(), stream=s)
     if why:
-        raise SystemExit(f"prepare_grad refused the workload: {why}")
+        raise SystemExit(f"prepare refused the workload: {why}")
     offs = np.concatenate([[0], np.cumsum(group_m)]).tolist()
 
     def cublas_step(dst):
         for g in range(ng):
             a, b = offs[g], offs[g + 1]
-            if op == gg.OP_DGRAD:
-                torch.matmul(dy[a:b], b_op[g], out=dst[a:b])
+            if op == gg.OP_FORWARD:
+                if b > a:
+                    torch.matmul(a_op[a:b], b_op[g].t(), out=dst[a:b])
+            elif op == gg.OP_DGRAD:
+                if b > a:
+                    torch.matmul(a_op[a:b], b_op[g], out=dst[a:b])
+            elif b > a:
+                torch.matmul(a_op[a:b].t(), b_op[a:b], out=dst[g])
             else:
-                torch.matmul(dy[a:b].t(), b_op[a:b], out=dst[g])
+                dst[g].zero_()  # an expert without tokens: dw[g] = 0, as the kernel writes
 
-    def timed(fn, steps):
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
+    ref = torch.empty_like(out)
+    # The loop is replayed from a CUDA graph, so its hundreds of small launches per step cost no
+    # host time (issued from Python one by one they can leave the GPU idle between experts).
+    with torch.cuda.stream(stream):
+        cublas_step(ref)  # cuBLAS workspace and handles before capture
+    torch.cuda.synchronize()
+    loop_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(loop_graph, stream=torch.cuda.Stream()):
+        cublas_step(ref)
+
+    def loop_replay():
+        loop_graph.replay()
+
+    arms = {"ours": lambda: be.run(s), "loop": loop_replay}
+    rounds = 5
+    per_round = max(2, args.steps // rounds)
+    ms_rounds = {a: [] for a in arms}
+    with torch.cuda.stream(stream):
+        for fn in arms.values():
             for _ in range(args.warmup):
                 fn()
-            torch.cuda.synchronize()
-            ev0.record(stream)
-            for _ in range(steps):
-                fn()
-            ev1.record(stream)
-        ev1.synchronize()
-        return ev0.elapsed_time(ev1) / steps
-
+    torch.cuda.synchronize()
     with ClockSampler(0) as clocks:
-        ms = timed(lambda: be.run(s), args.steps)
+        for _ in range(rounds):
+            for a, fn in arms.items():
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(stream):
+                    ev0.record(stream)
+                    for _ in range(per_round):
+                        fn()
+                    ev1.record(stream)
+                ev1.synchronize()
+                ms_rounds[a].append(ev0.elapsed_time(ev1) / per_round)
     if be.device_status(s) != 0:
         raise SystemExit("kernel reported a bounded-wait timeout")
-    ref = torch.empty_like(out)
-    ms_cublas = timed(lambda: cublas_step(ref), max(3, args.steps // 5))
-    # spot check against cuBLAS on the same tensors: the reference pass rule on every element
+    ms, ms_cublas = statistics.median(ms_rounds["ours"]), statistics.median(ms_rounds["loop"])
+    # check against cuBLAS on the same tensors: the reference pass rule on every element checked
     with torch.cuda.stream(stream):
         be.run(s)
-        cublas_step(ref)
+        ref.zero_()
+        loop_replay()
     torch.cuda.synchronize()
+    del loop_graph
     lim = min(out.numel(), 1 << 26)  # the first 64M elements (bounded temporaries)
     o32, r32 = out.view(-1)[:lim].float(), ref.view(-1)[:lim].float()
     diff = (o32 - r32).abs()
@@ -396,21 +437,25 @@ def run_backward(args, cfg):
     value = flops / (ms * 1e-3) / 1e12
     peaks, peak_src = measured_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK["bf16_tflops"]))
+    what = {gg.OP_FORWARD: "out = x[g] @ w[g]^T", gg.OP_DGRAD: "dx = dy @ w[g]", gg.OP_WGRAD: "dw[g] = dy[g]^T @ x[g]"}
     line = {
-        "metric": f"grouped-GEMM TFLOPS/GPU ({cfg['dtype']}), backward {args.op}", "op": args.op,
-        "value": round(value, 2), "unit": "TFLOPS", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "metric": f"grouped-GEMM TFLOPS/GPU ({cfg['dtype']}), {args.op} beside a per-expert cuBLAS loop",
+        "op": args.op, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": 1,
+        "steps": rounds * per_round, "warmup": args.warmup, "rounds": rounds,
         "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": cfg["dtype"],
         "data": "synthetic N(0,1) (torch generator on the device)",
-        "config": {"workload": cfg["desc"], "op": ("dx = dy @ w[g]" if op == gg.OP_DGRAD
-                                                   else "dw[g] = dy[g]^T @ x[g]"),
+        "config": {"workload": cfg["desc"], "op": what[op],
                    "l2": "inputs larger than L2 (no flush)" if rows * (n + k) * 2 > 126e6 else "inputs may fit in L2"},
         "roofline": {"bound": "tensor", "achieved": round(value, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(value / peak, 4), "peak_source": f"{peak_src} bf16 burst (cuBLAS)"},
         "cublas_loop": {"value": round(flops / (ms_cublas * 1e-3) / 1e12, 2), "unit": "TFLOPS",
-                        "ms_per_step": round(ms_cublas, 4), "how": "torch.matmul per expert, one stream"},
+                        "ms_per_step": round(ms_cublas, 4),
+                        "how": "torch.matmul per expert, one stream, replayed from a CUDA graph"},
+        "ratio_vs_loop": round(ms_cublas / ms, 3),
+        "rounds_tflops": {a: [round(flops / (v * 1e-3) / 1e12) for v in ms_rounds[a]] for a in arms},
         "check_vs_cublas": {"elements": int(lim), "outside_tolerance": bad,
                             "max_abs_diff": float(diff.max().item())},
-        "gpu_launches": args.steps, "clocks": clocks.summary(), "detail": be.detail(),
+        "gpu_launches": rounds * per_round, "clocks": clocks.summary(), "detail": be.detail(),
     }
     be.release()
     print(json.dumps(line), flush=True)
@@ -650,13 +695,17 @@ def main():
     ap.add_argument("--opt", action="append", default=[], metavar="KEY=VALUE",
                     help="gg_set_option knob for the headline problem's handle (repeatable), e.g. sched=0")
     ap.add_argument("--op", default="forward", choices=["forward", "dgrad", "wgrad"],
-                    help="dgrad/wgrad: time a backward grouped GEMM on one GPU (not the headline line)")
+                    help="dgrad/wgrad: time a backward grouped GEMM on one GPU beside a per-expert "
+                         "cuBLAS loop (not the headline line)")
+    ap.add_argument("--vs-loop", action="store_true",
+                    help="with --op forward: the same one-GPU comparison with a per-expert cuBLAS loop "
+                         "in place of the headline line")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     if args.warmup < 3:
         args.warmup = 3  # timing rule: at least 3 warm-up steps
-    if args.op != "forward" and args.impl == "ours":
-        return run_backward(args, cfg)
+    if (args.op != "forward" or args.vs_loop) and args.impl == "ours":
+        return run_vs_loop(args, cfg)
 
     if args.impl == "reference":
         return run_reference(args, cfg)

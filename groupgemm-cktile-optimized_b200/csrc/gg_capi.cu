@@ -117,6 +117,8 @@ struct gg_handle {
     int opt_order = 0;  // planned tile order (wgrad with store-bound and tensor-bound groups): -1 auto, 0 off, 1 on
     int opt_half = 0;    // 1 on (half-height last tiles where a group allows), 0 off (default), -1 = on
     int opt_sched = 0;  // -1 auto (dynamic for multi-wave launches of whole tiles), 0 static, 1 dynamic
+    int opt_l2_a = 0;   // L2 eviction priority of the A / B operand loads (forward, dgrad):
+    int opt_l2_b = 0;   // 0 no hint, 1 evict_first, 2 evict_last
 
     // prepared state
     bool ready = false;
@@ -261,6 +263,10 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < -1 || value > 1)
             return fail(h, GG_ERR_ARG, "sched must be -1 (auto), 0 (static) or 1 (dynamic tile dispatch)");
         h->opt_sched = int(value);
+    } else if (!std::strcmp(key, "l2_a") || !std::strcmp(key, "l2_b")) {
+        if (value < 0 || value > 2)
+            return fail(h, GG_ERR_ARG, "%s must be 0 (no hint), 1 (evict_first) or 2 (evict_last)", key);
+        (key[3] == 'a' ? h->opt_l2_a : h->opt_l2_b) = int(value);
     } else if (!std::strcmp(key, "pdl")) {
         if (value != 0 && value != 1)
             return fail(h, GG_ERR_ARG, "pdl must be 0 or 1");
@@ -731,6 +737,8 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     kp.test_stall = h->opt_test_stall;
     kp.half_tiles = half_tiles && total_m > 0 ? 1 : 0;
     kp.mn_chunks = mn_chunks;
+    kp.l2_a = op == gg::kOpWgrad ? 0 : h->opt_l2_a;
+    kp.l2_b = op == gg::kOpWgrad ? 0 : h->opt_l2_b;
     kp.out_rows = int32_t(op == gg::kOpWgrad ? int64_t(G) * q.n : total_m) - h->opt_test_bounds;
     kp.ws_float4s = partials ? int64_t(h->ws_cap / 16) : 0;
     kp.ctr_entries = partials ? int32_t(h->counters_cap / sizeof(int32_t)) : 0;

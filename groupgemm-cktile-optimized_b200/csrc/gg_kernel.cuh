@@ -131,6 +131,8 @@ struct KernelParams {
     int32_t *tile_ctr;    // non-null: dynamic tile dispatch (whole tiles only: splits <= 1, no
                           // stream-K). Cluster c takes tile c first, then tile C + atomicAdd(tile_ctr, 1)
                           // until past the last tile; 0 between launches (the last fetch resets it)
+    int32_t l2_a;         // forward / dgrad: L2 eviction priority of the A loads (activations, dy):
+    int32_t l2_b;         // and of the B loads (weights): 0 no hint, 1 evict_first, 2 evict_last
     int32_t out_rows;     // rows of the output tensor (sum(M), or G * N for wgrad): debug checks
     int64_t ws_float4s;   // float4 entries of the split-K / stream-K workspace: debug checks
     int32_t ctr_entries;  // entries of the arrival-counter array: debug checks
@@ -510,6 +512,33 @@ __device__ __forceinline__ void load_3d(uint32_t dst, const void *map, uint32_t 
     else
         ptx::tma_load_3d_pair(dst, map, bar, c0, c1, c2, pred);
 }
+// The same with an L2 eviction-priority policy when `hinted` (KernelParams::l2_a / l2_b), without
+// one otherwise (a uniform branch: every lane of the warp takes the same side).
+template <int kCG>
+__device__ __forceinline__ void load_2d(uint32_t dst, const void *map, uint32_t bar, int c0, int c1, bool hinted,
+                                        uint64_t policy, uint32_t pred) {
+    if (!hinted)
+        load_2d<kCG>(dst, map, bar, c0, c1, pred);
+    else if constexpr (kCG == 1)
+        ptx::tma_load_2d_hint(dst, map, bar, c0, c1, policy, pred);
+    else
+        ptx::tma_load_2d_pair_hint(dst, map, bar, c0, c1, policy, pred);
+}
+template <int kCG>
+__device__ __forceinline__ void load_3d(uint32_t dst, const void *map, uint32_t bar, int c0, int c1, int c2,
+                                        bool hinted, uint64_t policy, uint32_t pred) {
+    if (!hinted)
+        load_3d<kCG>(dst, map, bar, c0, c1, c2, pred);
+    else if constexpr (kCG == 1)
+        ptx::tma_load_3d_hint(dst, map, bar, c0, c1, c2, policy, pred);
+    else
+        ptx::tma_load_3d_pair_hint(dst, map, bar, c0, c1, c2, policy, pred);
+}
+
+// L2 policy of an operand's loads: 1 evict_first, 2 evict_last (KernelParams::l2_a / l2_b).
+__device__ __forceinline__ uint64_t l2_load_policy(int hint) {
+    return hint == 2 ? ptx::l2_policy_evict_last() : ptx::l2_policy_evict_first();
+}
 
 constexpr int kMnBoxBytes = 64 * kBK * 2;  // one MN-major box: 64 MN x 64 K elements
 
@@ -637,6 +666,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             int fenced_g = -1;  // wgrad: group whose tensor maps the warp has acquired
             const int issue_lane = __ffs(__ballot_sync(0xffffffffu, issue)) - 1;
+            const uint64_t pol_a = l2_load_policy(p.l2_a), pol_b = l2_load_policy(p.l2_b);
             int fetched = 0;  // dynamic dispatch, issuing lane of the leader: the next unit's fetch
             for (int i = 0; ok; ++i) {
                 Unit un;
@@ -749,17 +779,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     load_2d<kCG>(ad + kMnBoxBytes, map_a, fb, a_row + 64, k0, issue);
                                 }
                             } else {
-                                load_2d<kCG>(ad, half ? static_cast<const void *>(&tmap_a_half) : map_a, fb, k0, a_row, issue);
+                                load_2d<kCG>(ad, half ? static_cast<const void *>(&tmap_a_half) : map_a, fb, k0, a_row,
+                                             p.l2_a != 0, pol_a, issue);
                             }
                             if constexpr (kOp == kOpForward) {
-                                load_3d<kCG>(bd, map_b, fb, k0, b_row, tc.g, issue);
+                                load_3d<kCG>(bd, map_b, fb, k0, b_row, tc.g, p.l2_b != 0, pol_b, issue);
                             } else if (kOp == kOpWgrad && (p.mn_chunks & 2)) {
                                 // x rows (tokens) k0.. of the group, all b_rows / 64 chunks at once
                                 load_3d<kCG>(bd, map_b, fb, 0, k0, b_row / 64, issue);
                             } else {
                                 for (int j = 0; j < b_rows / 64; ++j) {
                                     if constexpr (kOp == kOpDgrad)  // w[g] rows k0.., columns b_row + 64j..
-                                        load_3d<kCG>(bd + j * kMnBoxBytes, map_b, fb, b_row + 64 * j, k0, tc.g, issue);
+                                        load_3d<kCG>(bd + j * kMnBoxBytes, map_b, fb, b_row + 64 * j, k0, tc.g,
+                                                     p.l2_b != 0, pol_b, issue);
                                     else  // x rows (tokens) k0.. of the group, columns b_row + 64j..
                                         load_2d<kCG>(bd + j * kMnBoxBytes, map_b, fb, b_row + 64 * j, k0, issue);
                                 }

@@ -182,6 +182,44 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void *tmap,
                  : "memory");
 }
 
+// The same four loads with an L2 eviction-priority hint (`policy` from l2_policy_*): the lines a
+// load brings into L2 are kept longer (evict_last) or dropped first (evict_first).
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const void *tmap, uint32_t bar, int32_t c0,
+                                                 int32_t c1, uint64_t policy, uint32_t pred) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+                 "@q cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+                 " [%0], [%1, {%3, %4}], [%2], %6;\n\t}" ::"r"(dst),
+                 "l"(tmap), "r"(bar), "r"(c0), "r"(c1), "r"(pred), "l"(policy)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_hint(uint32_t dst, const void *tmap, uint32_t bar, int32_t c0,
+                                                 int32_t c1, int32_t c2, uint64_t policy, uint32_t pred) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %6, 0;\n\t"
+                 "@q cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+                 " [%0], [%1, {%3, %4, %5}], [%2], %7;\n\t}" ::"r"(dst),
+                 "l"(tmap), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(pred), "l"(policy)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair_hint(uint32_t dst, const void *tmap, uint32_t bar, int32_t c0,
+                                                      int32_t c1, uint64_t policy, uint32_t pred) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+                 "@q cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %6;\n\t}" ::"r"(dst),
+                 "l"(tmap), "r"(bar), "r"(c0), "r"(c1), "r"(pred), "l"(policy)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair_hint(uint32_t dst, const void *tmap, uint32_t bar, int32_t c0,
+                                                      int32_t c1, int32_t c2, uint64_t policy, uint32_t pred) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %6, 0;\n\t"
+                 "@q cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 ".L2::cache_hint [%0], [%1, {%3, %4, %5}], [%2], %7;\n\t}" ::"r"(dst),
+                 "l"(tmap), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(pred), "l"(policy)
+                 : "memory");
+}
+
 // 32-byte streaming store (evict-first): the 16 bf16/fp16 values of one half-chunk of a row.
 // `p` must be 32-byte aligned.
 __device__ __forceinline__ void st_cs_v8(void *p, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -196,6 +234,18 @@ __device__ __forceinline__ void st_cs_v8(void *p, uint32_t a0, uint32_t a1, uint
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t pol;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
     return pol;
 }
 

@@ -159,6 +159,10 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
  *                dynamic for launches of whole tiles with more tiles than CTAs / pairs. The counter
  *                is zero between launches, so launches of one handle must not overlap on the GPU
  *                (order them on one stream, as for any handle)
+ *   "l2_a", "l2_b" forward / dgrad: L2 eviction priority of the A operand's (x, dy) and the B
+ *                operand's (weights) TMA loads: 0 no hint (default), 1 evict_first, 2 evict_last.
+ *                Results are unchanged; on B200 every hinted form measured slower on configs L, P
+ *                and D, so they are off unless asked for
  *   "tail_launch" -1 auto (default), 0 off, 1 on: with the 2-CTA variant (forward and dgrad, no
  *                split-K or stream-K), the rows of each group's last 256-row tile, where they are at
  *                most 128, go to a second launch of the one-CTA kernel (128-row tiles) right behind

@@ -233,3 +233,24 @@ def test_config_l_size_two_experts_vs_torch_fp32(gg, name):
         bad = ((got - ref).abs() > 1e-2 + 1e-2 * ref.abs()) | torch.isnan(got)
         assert int(bad.sum()) == 0, (name, g, int(bad.sum()), float((got - ref).abs().max()))
     b.release()
+
+
+@pytest.mark.parametrize("args", [["--op", "forward", "--vs-loop"], ["--op", "dgrad"], ["--op", "wgrad"]])
+def test_bench_vs_loop_leg(args):
+    """bench.py's one-GPU comparison leg (each op beside a per-expert cuBLAS loop, the two arms
+    alternating in rounds) on config T: one JSON line whose output agrees with cuBLAS everywhere."""
+    import json
+    import os
+    import subprocess
+    import sys
+
+    _torch()
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--config", "T", "--steps", "10",
+                        "--warmup", "3", *args], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["op"] == args[1] and line["rounds"] == 5 and line["gpu_launches"] == 10
+    assert line["check_vs_cublas"]["outside_tolerance"] == 0
+    assert line["value"] > 0 and line["cublas_loop"]["value"] > 0 and line["ratio_vs_loop"] > 0
+    assert len(line["rounds_tflops"]["ours"]) == len(line["rounds_tflops"]["loop"]) == 5

@@ -841,3 +841,56 @@ def test_forward_dgrad_interleaved_tile_order(gg, orc, opts, op):
         results[order] = runs[0]
         b.release()
     assert np.array_equal(results[0], results[1])
+
+
+@pytest.mark.parametrize("opts", [
+    {"variant": 0, "bn": 256},
+    {"variant": 0, "bn": 128, "split": 3},
+    {"variant": 0, "half_tiles": 1, "tail_launch": 0},
+    {"variant": 0, "tail_launch": 1, "max_ctas": 12},
+    {"variant": 1, "bn": 192, "sched": 1, "split": 1},
+    {"variant": 2, "bn": 64, "stream_k": 1, "max_ctas": 10},
+])
+@pytest.mark.parametrize("op", ["forward", "dgrad"])
+def test_l2_hints_same_bits(gg, orc, opts, op):
+    """L2 eviction-priority hints on the operand loads (options l2_a, l2_b) change only how long
+    lines stay in L2: every combination gives the bits of the unhinted launch and passes the
+    oracle's full compare."""
+    torch = _torch()
+    group_m, n, k = [300, 0, 17, 513, 129, 1000], 520, 1400
+    s = torch.cuda.current_stream().cuda_stream
+    up = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda()  # noqa: E731
+    if op == "forward":
+        x, w = orc.make_inputs(group_m, n, k, 0)
+        ref, rows, cols = orc.grouped_gemm_f32(x, w, group_m, 0), sum(group_m), n
+        xd, wd = up(x), up(w)
+    else:
+        dy, x, w = orc.make_grad_inputs(group_m, n, k, 0)
+        ref, rows, cols = orc.grouped_dgrad_f32(dy, w, group_m, 0), sum(group_m), k
+        dyd, wd = up(dy), up(w)
+    results = []
+    for l2_a, l2_b in ((0, 0), (2, 1), (1, 2), (2, 0)):
+        out = torch.full((rows * cols + GUARD,), CANARY, dtype=torch.int16, device="cuda")
+        b = gg.B200Backend()
+        for key, val in {**opts, "l2_a": l2_a, "l2_b": l2_b}.items():
+            b.set_option(key, val)
+        if op == "forward":
+            why = b.prepare(0, group_m, n, k, xd.data_ptr(), wd.data_ptr(), out.data_ptr(), s)
+        else:
+            why = b.prepare_grad(gg.OP_DGRAD, 0, group_m, n, k, dy_ptr=dyd.data_ptr(), w_ptr=wd.data_ptr(),
+                                 dx_ptr=out.data_ptr(), stream=s)
+        assert why == "", why
+        runs = []
+        for _ in range(2):
+            out[:rows * cols].fill_(0)
+            b.run(s)
+            assert b.device_status(s) == 0, b.detail()
+            res = out.cpu().numpy().view(np.uint16)
+            assert np.all(res[rows * cols:] == CANARY), (b.detail(), "store past the end of out")
+            runs.append(res[:rows * cols].reshape(rows, cols).copy())
+        assert np.array_equal(runs[0], runs[1]), b.detail()
+        bad, mx, first = orc.check16(runs[0], ref, 0)
+        assert bad == 0, (b.detail(), l2_a, l2_b, bad, mx, first)
+        results.append(runs[0])
+        b.release()
+    assert all(np.array_equal(results[0], r) for r in results[1:])
