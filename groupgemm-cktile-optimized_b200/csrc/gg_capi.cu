@@ -117,8 +117,8 @@ struct gg_handle {
     int opt_order = 0;  // planned tile order (wgrad with store-bound and tensor-bound groups): -1 auto, 0 off, 1 on
     int opt_half = 0;    // 1 on (half-height last tiles where a group allows), 0 off (default), -1 = on
     int opt_sched = 0;  // -1 auto (dynamic for multi-wave launches of whole tiles), 0 static, 1 dynamic
-    int opt_l2_a = 0;   // L2 eviction priority of the A / B operand loads (forward, dgrad):
-    int opt_l2_b = 0;   // 0 no hint, 1 evict_first, 2 evict_last
+    int opt_l2_a = -1;  // L2 eviction priority of the A / B operand loads (forward, dgrad):
+    int opt_l2_b = 0;   // 0 no hint, 1 evict_first, 2 evict_last; l2_a -1 = automatic
 
     // prepared state
     bool ready = false;
@@ -263,10 +263,14 @@ int gg_set_option(gg_handle *h, const char *key, int64_t value) {
         if (value < -1 || value > 1)
             return fail(h, GG_ERR_ARG, "sched must be -1 (auto), 0 (static) or 1 (dynamic tile dispatch)");
         h->opt_sched = int(value);
-    } else if (!std::strcmp(key, "l2_a") || !std::strcmp(key, "l2_b")) {
+    } else if (!std::strcmp(key, "l2_a")) {
+        if (value < -1 || value > 2)
+            return fail(h, GG_ERR_ARG, "l2_a must be -1 (auto), 0 (no hint), 1 (evict_first) or 2 (evict_last)");
+        h->opt_l2_a = int(value);
+    } else if (!std::strcmp(key, "l2_b")) {
         if (value < 0 || value > 2)
-            return fail(h, GG_ERR_ARG, "%s must be 0 (no hint), 1 (evict_first) or 2 (evict_last)", key);
-        (key[3] == 'a' ? h->opt_l2_a : h->opt_l2_b) = int(value);
+            return fail(h, GG_ERR_ARG, "l2_b must be 0 (no hint), 1 (evict_first) or 2 (evict_last)");
+        h->opt_l2_b = int(value);
     } else if (!std::strcmp(key, "pdl")) {
         if (value != 0 && value != 1)
             return fail(h, GG_ERR_ARG, "pdl must be 0 or 1");
@@ -737,7 +741,18 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     kp.test_stall = h->opt_test_stall;
     kp.half_tiles = half_tiles && total_m > 0 ? 1 : 0;
     kp.mn_chunks = mn_chunks;
-    kp.l2_a = op == gg::kOpWgrad ? 0 : h->opt_l2_a;
+    // L2 policy of the operand loads. Automatic: where the weights outweigh the activations at
+    // least 4 : 1 (few tokens per expert, many experts: config E) and the launch runs at least 64
+    // waves, the weights stream through L2 once while the clusters drift apart, and they push out
+    // activation rows that later n-tiles of the same expert still read; those loads are marked
+    // evict_last. Measured (interleaved, 8 rounds): E (110 waves) +9.5%; its 2-, 4- and 8-GPU
+    // shares (55 / 28 / 14 waves) unchanged within noise, so they keep no hint; L / P / D slower.
+    const double act_elems = double(total_m) * double(kp.k);
+    const double w_elems = double(G) * double(q.n) * double(q.k);
+    const bool long_launch = tiles >= 64 * int64_t(std::max(1, h->grid / v.cg));
+    kp.l2_a = op == gg::kOpWgrad ? 0
+              : h->opt_l2_a >= 0 ? h->opt_l2_a
+                                 : (w_elems >= 4.0 * act_elems && long_launch ? 2 : 0);
     kp.l2_b = op == gg::kOpWgrad ? 0 : h->opt_l2_b;
     kp.out_rows = int32_t(op == gg::kOpWgrad ? int64_t(G) * q.n : total_m) - h->opt_test_bounds;
     kp.ws_float4s = partials ? int64_t(h->ws_cap / 16) : 0;
@@ -860,14 +875,16 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     h->fn = fn;
     h->smem = v.smem;
     h->cg = v.cg;
-    char form[160];
+    char form[224];
     if (sk_tiles > 0)
         std::snprintf(form, sizeof(form), "split=1 stream_k=%lld tiles(<=%d pieces)", (long long)sk_tiles, ch.splits);
     else
-        std::snprintf(form, sizeof(form), "split=%d%s%s%s%s%s", ch.splits,
+        std::snprintf(form, sizeof(form), "split=%d%s%s%s%s%s%s%s", ch.splits,
                       split_tiles > 0 && split_tiles < tiles ? "(last wave)" : "", dynamic ? " dynamic" : "",
                       half_tiles ? " half-tiles" : "", planned ? " interleaved" : "",
-                      mn_chunks == 3 ? " chunk-boxes" : mn_chunks == 1 ? " chunk-boxes(dy)" : mn_chunks == 2 ? " chunk-boxes(x)" : "");
+                      mn_chunks == 3 ? " chunk-boxes" : mn_chunks == 1 ? " chunk-boxes(dy)" : mn_chunks == 2 ? " chunk-boxes(x)" : "",
+                      kp.l2_a == 2 ? " a:evict_last" : kp.l2_a == 1 ? " a:evict_first" : "",
+                      kp.l2_b == 2 ? " b:evict_last" : kp.l2_b == 1 ? " b:evict_first" : "");
     char tail_form[96] = "";
     if (h->tail.active)
         std::snprintf(tail_form, sizeof(tail_form), " +tail gg_sm100 tile=128x%d cta_group=1 tiles=%lld grid=%d", bn,

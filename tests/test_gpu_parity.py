@@ -894,3 +894,20 @@ def test_l2_hints_same_bits(gg, orc, opts, op):
         results.append(runs[0])
         b.release()
     assert all(np.array_equal(results[0], r) for r in results[1:])
+
+
+def test_l2_hint_automatic_choice(gg, orc):
+    """The automatic L2 policy (l2_a = -1, the default) marks the activation loads evict_last only
+    where the weights outweigh the activations at least 4 : 1 and the launch runs at least 64
+    waves (here: a grid capped at 2 clusters), and the result is the oracle's."""
+    torch = _torch()
+    cases = (([64] * 8, 1024, 512, {"max_ctas": 2, "variant": 1, "bn": 64}, True),
+             ([64] * 8, 1024, 512, {}, False),
+             ([2048, 2048], 512, 512, {"max_ctas": 2, "variant": 1, "bn": 64}, False))
+    for group_m, n, k, opts, want in cases:
+        x, w = orc.make_inputs(group_m, n, k, 0)
+        ref = orc.grouped_gemm_f32(x, w, group_m, 0)
+        res, detail = _run_opts(gg, torch, group_m, n, k, 0, upload(torch, x), upload(torch, w), opts)
+        assert ("a:evict_last" in detail) == want, detail
+        bad, mx, first = orc.check16(res[0], ref, 0)
+        assert bad == 0, (detail, bad, mx, first)
