@@ -78,12 +78,14 @@ def test_set_option(gg):
                      ("stream_k", 0), ("stream_k", 1), ("stream_k", 2), ("bn", 240), ("bn", 16), ("bn", 0),
                      ("sched", -1), ("sched", 0), ("sched", 1), ("half_tiles", -1), ("half_tiles", 0), ("half_tiles", 1),
                      ("tail_launch", -1), ("tail_launch", 0), ("tail_launch", 1), ("test_bounds", 0), ("test_bounds", 1),
-                     ("tile_order", -1), ("tile_order", 0), ("tile_order", 1), ("tma_chunks", 0), ("tma_chunks", 1)):
+                     ("tile_order", -1), ("tile_order", 0), ("tile_order", 1), ("tma_chunks", 0), ("tma_chunks", 1),
+                     ("l2_a", -1), ("l2_a", 0), ("l2_a", 2), ("l2_b", 0), ("l2_b", 1), ("l2_b", 2)):
         b.set_option(key, val)
     for key, val in (("variant", 7), ("band", -1), ("timeout_ms", 0), ("test_stall", 2), ("bn", 100), ("bn", 288), ("split", 9),
                      ("split_tail", 2), ("raster", 2), ("pdl", 3), ("store", 2), ("bogus", 1), ("bn", 24), ("bn", 8),
                      ("stream_k", 3), ("stream_k", -2), ("sched", 2), ("sched", -2), ("half_tiles", 2), ("tail_launch", 2), ("test_bounds", 2),
-                     ("tile_order", 2), ("tile_order", -2), ("tma_chunks", 2), ("tma_chunks", -1)):
+                     ("tile_order", 2), ("tile_order", -2), ("tma_chunks", 2), ("tma_chunks", -1), ("l2_a", 3), ("l2_a", -2),
+                     ("l2_b", -1), ("l2_b", 3)):
         with pytest.raises(gg.GGError):
             b.set_option(key, val)
 

@@ -682,7 +682,8 @@ def test_half_height_tiles_with_dynamic_dispatch_and_graph(gg, orc):
 def test_split_launch_for_skewed_routing(gg, orc, dtype, op, group_m):
     """With the 2-CTA variant, groups whose last pair tile would hold at most 128 rows hand those
     rows to a second launch of the one-CTA kernel (tail_launch). Full compare against the oracle
-    with the split on and off, two runs each, and in a captured CUDA graph."""
+    with the split on and off: two runs each, three launches back to back, and a captured CUDA
+    graph of two launches; the split gives the unsplit bits."""
     torch = _torch()
     n, k = 8 * 97, 200 if op == "forward" else 8 * 50
     s = torch.cuda.current_stream().cuda_stream
@@ -696,6 +697,7 @@ def test_split_launch_for_skewed_routing(gg, orc, dtype, op, group_m):
         ref, cols = orc.grouped_dgrad_f32(dy, w, group_m, dtype), k
         dyd, wd = up(dy), up(w)
     rows = sum(group_m)
+    results = {}
     for split in (1, 0):
         out = torch.full((rows * cols + GUARD,), CANARY, dtype=torch.int16, device="cuda")
         b = gg.B200Backend()
@@ -708,19 +710,22 @@ def test_split_launch_for_skewed_routing(gg, orc, dtype, op, group_m):
                                  dx_ptr=out.data_ptr(), stream=s)
         assert why == "", why
         assert ("+tail" in b.detail()) == bool(split), b.detail()
-        for _ in range(2):
+        for reps in (1, 1, 3):
             out[:rows * cols].fill_(0)
-            b.run(s)
+            for _ in range(reps):
+                b.run(s)
             assert b.device_status(s) == 0, b.detail()
             res = out.cpu().numpy().view(np.uint16)
             assert np.all(res[rows * cols:] == CANARY), (b.detail(), "store past the end of out")
             bad, mx, first = orc.check16(res[:rows * cols].reshape(rows, cols), ref, dtype)
             assert bad == 0, (b.detail(), bad, mx, divmod(first, cols) if first >= 0 else first)
+        results[split] = res[:rows * cols].copy()
         if split:
             st = torch.cuda.Stream()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=st):
-                b.run(torch.cuda.current_stream().cuda_stream)
+                for _ in range(2):
+                    b.run(torch.cuda.current_stream().cuda_stream)
             out[:rows * cols].fill_(0)
             torch.cuda.synchronize()
             g.replay()
@@ -728,7 +733,9 @@ def test_split_launch_for_skewed_routing(gg, orc, dtype, op, group_m):
             assert b.device_status(s) == 0
             bad, _, _ = orc.check16(out.cpu().numpy().view(np.uint16)[:rows * cols].reshape(rows, cols), ref, dtype)
             assert bad == 0, (b.detail(), "graph replay")
+            del g
         b.release()
+    assert np.array_equal(results[1], results[0])
 
 
 @pytest.mark.parametrize("sched", [0, 1])
