@@ -117,7 +117,7 @@ struct gg_handle {
     int opt_order = 0;  // planned tile order (wgrad with store-bound and tensor-bound groups): -1 auto, 0 off, 1 on
     int opt_half = 0;    // 1 on (half-height last tiles where a group allows), 0 off (default), -1 = on
     int opt_sched = 0;  // -1 auto (dynamic for multi-wave launches of whole tiles), 0 static, 1 dynamic
-    int opt_l2_a = -1;  // L2 eviction priority of the A / B operand loads (forward, dgrad):
+    int opt_l2_a = -1;  // L2 eviction priority of the A / B operand loads (forward):
     int opt_l2_b = 0;   // 0 no hint, 1 evict_first, 2 evict_last; l2_a -1 = automatic
 
     // prepared state
@@ -750,10 +750,10 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     const double act_elems = double(total_m) * double(kp.k);
     const double w_elems = double(G) * double(q.n) * double(q.k);
     const bool long_launch = tiles >= 64 * int64_t(std::max(1, h->grid / v.cg));
-    kp.l2_a = op == gg::kOpWgrad ? 0
+    kp.l2_a = op != gg::kOpForward ? 0
               : h->opt_l2_a >= 0 ? h->opt_l2_a
                                  : (w_elems >= 4.0 * act_elems && long_launch ? 2 : 0);
-    kp.l2_b = op == gg::kOpWgrad ? 0 : h->opt_l2_b;
+    kp.l2_b = op != gg::kOpForward ? 0 : h->opt_l2_b;
     kp.out_rows = int32_t(op == gg::kOpWgrad ? int64_t(G) * q.n : total_m) - h->opt_test_bounds;
     kp.ws_float4s = partials ? int64_t(h->ws_cap / 16) : 0;
     kp.ctr_entries = partials ? int32_t(h->counters_cap / sizeof(int32_t)) : 0;

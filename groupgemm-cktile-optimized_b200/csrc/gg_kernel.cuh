@@ -131,7 +131,7 @@ struct KernelParams {
     int32_t *tile_ctr;    // non-null: dynamic tile dispatch (whole tiles only: splits <= 1, no
                           // stream-K). Cluster c takes tile c first, then tile C + atomicAdd(tile_ctr, 1)
                           // until past the last tile; 0 between launches (the last fetch resets it)
-    int32_t l2_a;         // forward / dgrad: L2 eviction priority of the A loads (activations, dy):
+    int32_t l2_a;         // forward: L2 eviction priority of the A loads (activations):
     int32_t l2_b;         // and of the B loads (weights): 0 no hint, 1 evict_first, 2 evict_last
     int32_t out_rows;     // rows of the output tensor (sum(M), or G * N for wgrad): debug checks
     int64_t ws_float4s;   // float4 entries of the split-K / stream-K workspace: debug checks
@@ -779,8 +779,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     load_2d<kCG>(ad + kMnBoxBytes, map_a, fb, a_row + 64, k0, issue);
                                 }
                             } else {
-                                load_2d<kCG>(ad, half ? static_cast<const void *>(&tmap_a_half) : map_a, fb, k0, a_row,
-                                             p.l2_a != 0, pol_a, issue);
+                                // the L2 policy form only in the forward op: in the dgrad producer the
+                                // hinted form cost more than any hint saved (dgrad L -10%)
+                                if constexpr (kOp == kOpForward)
+                                    load_2d<kCG>(ad, half ? static_cast<const void *>(&tmap_a_half) : map_a, fb, k0, a_row,
+                                                 p.l2_a != 0, pol_a, issue);
+                                else
+                                    load_2d<kCG>(ad, half ? static_cast<const void *>(&tmap_a_half) : map_a, fb, k0, a_row, issue);
                             }
                             if constexpr (kOp == kOpForward) {
                                 load_3d<kCG>(bd, map_b, fb, k0, b_row, tc.g, p.l2_b != 0, pol_b, issue);
@@ -790,8 +795,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             } else {
                                 for (int j = 0; j < b_rows / 64; ++j) {
                                     if constexpr (kOp == kOpDgrad)  // w[g] rows k0.., columns b_row + 64j..
-                                        load_3d<kCG>(bd + j * kMnBoxBytes, map_b, fb, b_row + 64 * j, k0, tc.g,
-                                                     p.l2_b != 0, pol_b, issue);
+                                        load_3d<kCG>(bd + j * kMnBoxBytes, map_b, fb, b_row + 64 * j, k0, tc.g, issue);
                                     else  // x rows (tokens) k0.. of the group, columns b_row + 64j..
                                         load_2d<kCG>(bd + j * kMnBoxBytes, map_b, fb, b_row + 64 * j, k0, issue);
                                 }

@@ -159,13 +159,14 @@ int gg_device_status(gg_handle *h, gg_stream_t stream, uint32_t *status);
  *                dynamic for launches of whole tiles with more tiles than CTAs / pairs. The counter
  *                is zero between launches, so launches of one handle must not overlap on the GPU
  *                (order them on one stream, as for any handle)
- *   "l2_a", "l2_b" forward / dgrad: L2 eviction priority of the A operand's (x, dy) and the B
- *                operand's (weights) TMA loads: 0 no hint, 1 evict_first, 2 evict_last; l2_a -1
+ *   "l2_a", "l2_b" forward op: L2 eviction priority of the A operand's (x) and the B operand's
+ *                (weights) TMA loads: 0 no hint, 1 evict_first, 2 evict_last; l2_a -1
  *                (its default) = evict_last where the launch's weights outweigh its activations at
  *                least 4 : 1 and it runs at least 64 waves of tiles (many experts with few tokens
  *                each: over a long launch the streaming weights would push out activation rows
  *                that later tiles of the expert still read), no hint otherwise; l2_b defaults to 0.
- *                Results are unchanged by either
+ *                Results are unchanged by either. Backward operations ignore both (in the dgrad
+ *                producer the hinted load form measured slower than any hint saved)
  *   "tail_launch" -1 auto (default), 0 off, 1 on: with the 2-CTA variant (forward and dgrad, no
  *                split-K or stream-K), the rows of each group's last 256-row tile, where they are at
  *                most 128, go to a second launch of the one-CTA kernel (128-row tiles) right behind
