@@ -745,7 +745,8 @@ int prepare_op(gg_handle *h, const OpProblem &q, gg_stream_t stream, char *why, 
     // least 4 : 1 (few tokens per expert, many experts: config E) and the launch runs at least 64
     // waves, the weights stream through L2 once while the clusters drift apart, and they push out
     // activation rows that later n-tiles of the same expert still read; those loads are marked
-    // evict_last. Measured (interleaved, 8 rounds): E (110 waves) +9.5%; its 2-, 4- and 8-GPU
+    // evict_last. Measured (interleaved, 8-10 rounds, both orders on one box): E (110 waves) +9.5%
+    // on two boxes, +0.6% on a third that ran E power-capped at ~1100 TFLOPS; its 2-, 4- and 8-GPU
     // shares (55 / 28 / 14 waves) unchanged within noise, so they keep no hint; L / P / D slower.
     const double act_elems = double(total_m) * double(kp.k);
     const double w_elems = double(G) * double(q.n) * double(q.k);
