@@ -44,7 +44,7 @@ TARGETS = {
     },
     "gg_bench": {
         "srcs": ["gg_bench_main.cu", "gg_cublas_backends.cpp", "gg_capi.cu"],
-        "deps": ["gg_bench_main.cu", "gg_cublas_backends.cpp", "gg_capi.cu", "gg_kernel.cuh", "gg_ptx.cuh",
+        "deps": ["gg_bench_main.cu", "gg_cublas_backends.cpp", "gg_capi.cu", "gg_kernel.cuh", "gg_ptx.cuh", "gg_sched.h",
                  os.path.join("..", "..", "include", "gg_backend.hpp")],
         "flags": ["-lcublas"],
     },

@@ -142,9 +142,12 @@ inline Choice choose_tiling(const TileShape *shapes, int nshapes, const gg_probl
             if (forced_bn <= 0 && bn < 128 && tiles_for(p, v, bn) > slots)
                 continue;  // below 128 columns only for a one-wave tiling (it fills more SMs)
             // A width in steps of 16 (not 32) only where it tiles N exactly (N = 2880 = 12 x 240
-            // against 256's 6.7% padding: +2-9% measured); with a ragged N tail it measured
-            // between -5% and +3% against the widths in steps of 32.
-            if (forced_bn <= 0 && bn % 32 != 0 && p->n % bn != 0)
+            // against 256's 6.7% padding: +2-9% measured), or where a width of at least 160 fits
+            // the launch in one wave (one tile per CTA or pair: 1 x 512 x 6144 x 16384 as 70 pairs
+            // of 256 x 176 +5.5% over 3-way split-K, 240-wide one-CTA and pair tilings of four more
+            // single-wave suite shapes +0.6-2.4%); with a ragged N tail over several waves it
+            // measured between -5% and +3% against the widths in steps of 32.
+            if (forced_bn <= 0 && bn % 32 != 0 && p->n % bn != 0 && !(bn >= 160 && tiles_for(p, v, bn) <= slots))
                 continue;
             if (mn_major_b && (bn / v.cg) % 64 != 0)
                 continue;  // MN-major B is loaded in 64-column boxes

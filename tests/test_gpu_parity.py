@@ -918,3 +918,19 @@ def test_l2_hint_automatic_choice(gg, orc):
         assert ("a:evict_last" in detail) == want, detail
         bad, mx, first = orc.check16(res[0], ref, 0)
         assert bad == 0, (detail, bad, mx, first)
+
+
+@pytest.mark.parametrize("group_m,n,k", [([512], 6144, 1024), ([1024], 3000, 512)])
+def test_automatic_ragged_one_wave_width(gg, orc, group_m, n, k):
+    """The automatic choice takes a width in steps of 16 that does not divide N where it fits the
+    launch in one wave (here 176 columns: a ragged last n-tile on every m-tile). Full compare
+    against the oracle, two launches in a row with the same bits, nothing stored past out."""
+    torch = _torch()
+    x, w = orc.make_inputs(group_m, n, k, 0)
+    ref = orc.grouped_gemm_f32(x, w, group_m, 0)
+    res, detail = _run_opts(gg, torch, group_m, n, k, 0, upload(torch, x), upload(torch, w), {})
+    bn = int(detail.split(" tile=")[1].split("x")[1])
+    assert bn % 32 == 16 and n % bn != 0, detail
+    assert np.array_equal(res[0], res[1]), detail
+    bad, mx, first = orc.check16(res[0], ref, 0)
+    assert bad == 0, (detail, bad, mx, first)

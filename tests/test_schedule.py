@@ -48,8 +48,10 @@ def test_schedule_covers_every_atom_once_and_summer_never_waits_in_a_cycle(sched
 # The cost model's automatic choices on the BASELINE shapes, each the measured best of the
 # alternatives tried on a B200 (interleaved A/B runs): pair 256 x 256 tiles for L, D and E, pair
 # 256 x 240 for P (12 x 240 = 2880, no N padding), one wave of 144 one-CTA 128 x 160 tiles for the
-# B=1 variant of P, one-CTA 128 x 96 tiles for T, and 256 x 256 with the partial last wave split 3
-# ways in K for W. A model change that moves one of these must come with new measurements.
+# B=1 variant of P, one-CTA 128 x 96 tiles for T, 256 x 256 with the partial last wave split 3
+# ways in K for W, and one wave of 70 pairs of 256 x 176 tiles for the suite's single-expert
+# 1 x 512 x 6144 x 16384 (+5.5% over 3-way split-K). A model change that moves one of these must
+# come with new measurements.
 PINNED = {
     "8,4096,4096,7168": (0, 256, 1, 0, 0),     # L
     "32,2048,7168,2048": (0, 256, 1, 0, 0),    # D
@@ -58,6 +60,7 @@ PINNED = {
     "1,1000,2880,2880": (1, 160, 1, 0, 0),     # P, B=1
     "4,256,512,384": (2, 96, 1, 0, 0),         # T
     "2,512,6144,8192": (0, 256, 3, 1, 0),      # W (last-wave split)
+    "1,512,6144,16384": (0, 176, 1, 0, 0),     # suite TestID 278: one wave of 70 pairs, no split
 }
 
 
@@ -73,8 +76,9 @@ def test_cost_model_keeps_the_measured_best_choices(sched_check):
 
 
 def test_cost_model_width_rules_hold_on_many_shapes(sched_check):
-    # widths in steps of 16; a width that is not a multiple of 32 only where it tiles N exactly;
-    # below 128 columns only when the tiling fits in one wave; stream-K never by default
+    # widths in steps of 16; a width that is not a multiple of 32 only where it tiles N exactly
+    # or, at 160 columns or more, fits the launch in one wave; below 128 columns only when the
+    # tiling fits in one wave; stream-K never by default
     import itertools
     shapes = [f"{b},{m},{n},{k}" for b, m, n, k in itertools.product(
         (1, 2, 4, 8, 16, 64), (256, 512, 1000, 2048, 8192), (512, 1536, 2816, 2880, 4096, 5760, 7168),
@@ -82,9 +86,10 @@ def test_cost_model_width_rules_hold_on_many_shapes(sched_check):
     for shape, (variant, bn, splits, hybrid, sk) in zip(shapes, _choose(sched_check, shapes)):
         b, m, n, k = (int(v) for v in shape.split(","))
         assert bn % 16 == 0 and sk == 0, shape
+        cluster_m = 256 if variant == 0 else 128
+        slots = 74 if variant == 0 else 148
+        one_wave = b * -(-m // cluster_m) * -(-n // bn) <= slots
         if bn % 32:
-            assert n % bn == 0, shape
+            assert n % bn == 0 or (bn >= 160 and one_wave), shape
         if bn < 128:
-            cluster_m = 256 if variant == 0 else 128
-            slots = 74 if variant == 0 else 148
-            assert b * -(-m // cluster_m) * -(-n // bn) <= slots, shape
+            assert one_wave, shape
